@@ -1,0 +1,399 @@
+// fd_api.cu - the C ABI (include/flashdecode.h): argument checks, kernel
+// choice, tensor-map encoding, workspace ownership, error reporting.
+//
+// Host dispatch replaces the reference's run_kernel body
+// (submission-oj/best_flashattn_kvcache_decode.cu:1186-1426): instead of a
+// fixed split table chosen from (batch, max length) and a grow-only static
+// workspace shared by every device and stream, the split is decided on the
+// device from cache_seqlens (stream-K ranges, see fd_decode_sm100.cu) and the
+// workspace is either the caller's or a per-device buffer.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/flashdecode.h"
+#include "fd_kernels.h"
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr unsigned long long kDefaultTimeoutNs = 1000000000ull;  // 1 s per in-kernel wait
+
+thread_local int t_last_error = FD_OK;
+thread_local char t_last_msg[256] = "ok";
+
+int set_error(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int set_error(int code, const char* fmt, ...) {
+  t_last_error = code;
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_msg, sizeof(t_last_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int set_ok() {
+  t_last_error = FD_OK;
+  std::strcpy(t_last_msg, "ok");
+  return FD_OK;
+}
+
+// ----------------------------------------------------------------- driver
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+struct DeviceState {
+  std::mutex mu;
+  int num_sms = 0;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+};
+DeviceState g_dev[kMaxDevices];
+
+int device_sms(int dev) {
+  DeviceState& s = g_dev[dev];
+  std::lock_guard<std::mutex> lk(s.mu);
+  if (s.num_sms == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    s.num_sms = n;
+  }
+  return s.num_sms;
+}
+
+// Library-owned workspace of `dev`: grow-only, zero-filled when (re)allocated.
+void* internal_workspace(int dev, size_t bytes, cudaStream_t stream) {
+  DeviceState& s = g_dev[dev];
+  std::lock_guard<std::mutex> lk(s.mu);
+  if (s.ws_bytes >= bytes) return s.ws;
+  if (s.ws != nullptr) {
+    cudaStreamSynchronize(stream);
+    cudaFree(s.ws);
+    s.ws = nullptr;
+    s.ws_bytes = 0;
+  }
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess) {
+    cudaFree(p);
+    return nullptr;
+  }
+  s.ws = p;
+  s.ws_bytes = bytes;
+  return p;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int esize(int dtype) { return dtype == FD_DTYPE_FP32 ? 4 : 2; }
+
+int pick_chunk(int64_t page) {
+  if (page % 128 == 0) return 128;
+  if (page % 64 == 0) return 64;
+  if (page % 32 == 0) return 32;
+  if (page % 16 == 0) return 16;
+  return 0;
+}
+
+CUresult encode(CUtensorMap* m, int dtype, int rank, const void* base, const cuuint64_t* dims,
+                const cuuint64_t* strides, const cuuint32_t* box) {
+  const cuuint32_t estride[5] = {1, 1, 1, 1, 1};
+  return encode_fn()(m,
+                     dtype == FD_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                     static_cast<cuuint32_t>(rank), const_cast<void*>(base), dims, strides, box,
+                     estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+unsigned long long timeout_ns() {
+  static unsigned long long v = [] {
+    const char* e = std::getenv("FD_WAIT_TIMEOUT_NS");
+    if (e != nullptr) {
+      const unsigned long long x = std::strtoull(e, nullptr, 10);
+      if (x > 0) return x;
+    }
+    return kDefaultTimeoutNs;
+  }();
+  return v;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* fd_version(void) { return "flashdecode-sm100 0.1.0"; }
+
+int fd_last_error(void) { return t_last_error; }
+
+const char* fd_last_error_message(void) { return t_last_msg; }
+
+const char* fd_error_string(int code) {
+  switch (code) {
+    case FD_OK: return "ok";
+    case FD_ERR_INVALID_ARG: return "invalid argument";
+    case FD_ERR_UNSUPPORTED: return "unsupported configuration";
+    case FD_ERR_WORKSPACE: return "workspace missing or too small";
+    case FD_ERR_CUDA: return "CUDA error";
+    case FD_ERR_DEVICE_TIMEOUT: return "in-kernel wait timed out";
+    default: return "unknown error";
+  }
+}
+
+size_t fd_decode_workspace_size(int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
+                                int64_t headdim) {
+  if (batch_size <= 0 || num_heads <= 0 || num_heads_k <= 0 || num_heads % num_heads_k != 0)
+    return 0;
+  (void)headdim;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices) return 0;
+  const int sms = device_sms(dev);
+  if (sms <= 0) return 0;
+  const int64_t nb = batch_size < fd::kMaxBatchPerLaunch ? batch_size : fd::kMaxBatchPerLaunch;
+  return fd::workspace_layout(nb, num_heads_k, num_heads / num_heads_k, sms).total;
+}
+
+int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, void* out, float* lse,
+                    const int32_t* cache_seqlens, const int32_t* block_table,
+                    int64_t block_table_stride, int64_t batch_size, int64_t num_heads,
+                    int64_t num_heads_k, int64_t headdim, int64_t page_block_size,
+                    int64_t num_blocks, int dtype, int out_dtype, float softmax_scale,
+                    int64_t max_seqlen_k, void* workspace, size_t workspace_bytes, void* stream) {
+  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr ||
+      cache_seqlens == nullptr || block_table == nullptr)
+    return set_error(FD_ERR_INVALID_ARG, "null tensor pointer");
+  if (batch_size <= 0 || num_heads <= 0 || num_heads_k <= 0 || page_block_size <= 0 ||
+      num_blocks <= 0 || block_table_stride <= 0)
+    return set_error(FD_ERR_INVALID_ARG,
+                     "sizes must be positive (batch=%lld heads=%lld kv_heads=%lld page=%lld "
+                     "num_blocks=%lld bt_stride=%lld)",
+                     (long long)batch_size, (long long)num_heads, (long long)num_heads_k,
+                     (long long)page_block_size, (long long)num_blocks,
+                     (long long)block_table_stride);
+  if (num_heads % num_heads_k != 0)
+    return set_error(FD_ERR_INVALID_ARG, "num_heads %lld not a multiple of num_heads_k %lld",
+                     (long long)num_heads, (long long)num_heads_k);
+  if (dtype != FD_DTYPE_BF16 && dtype != FD_DTYPE_FP16)
+    return set_error(FD_ERR_INVALID_ARG, "dtype must be bf16 or fp16");
+  if (out_dtype != dtype && out_dtype != FD_DTYPE_FP32)
+    return set_error(FD_ERR_INVALID_ARG, "out_dtype must equal dtype or be fp32");
+  if (!std::isfinite(softmax_scale))
+    return set_error(FD_ERR_INVALID_ARG, "softmax_scale must be finite");
+  if (headdim != 32 && headdim != 64 && headdim != 128 && headdim != 256)
+    return set_error(FD_ERR_UNSUPPORTED, "head dim %lld not in {32, 64, 128, 256}",
+                     (long long)headdim);
+  if (batch_size * num_heads > INT32_MAX || num_blocks > INT32_MAX ||
+      page_block_size > INT32_MAX || num_heads > 65535)
+    return set_error(FD_ERR_UNSUPPORTED, "size exceeds 32-bit index range");
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices)
+    return set_error(FD_ERR_CUDA, "no current CUDA device");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int group = static_cast<int>(num_heads / num_heads_k);
+  const float scale_log2 = softmax_scale * 1.4426950408889634f;
+  const bool out_fp32 = out_dtype == FD_DTYPE_FP32;
+  const int chunk = pick_chunk(page_block_size);
+
+  const bool tensor_core_path = headdim == fd::kHeadDim && group <= fd::kMaxGroup && chunk > 0 &&
+                                aligned16(q) && aligned16(k_cache) && aligned16(v_cache) &&
+                                encode_fn() != nullptr;
+  if (!tensor_core_path) {
+    fd::SimtParams sp;
+    sp.q = q; sp.k = k_cache; sp.v = v_cache; sp.out = out; sp.lse = lse;
+    sp.seqlens = cache_seqlens; sp.block_table = block_table; sp.bt_stride = block_table_stride;
+    sp.batch = static_cast<int>(batch_size); sp.num_heads = static_cast<int>(num_heads);
+    sp.num_heads_k = static_cast<int>(num_heads_k); sp.group = group;
+    sp.head_dim = static_cast<int>(headdim); sp.page = static_cast<int>(page_block_size);
+    sp.num_blocks = num_blocks; sp.scale_log2 = scale_log2;
+    const int vec = static_cast<int>(headdim / 32) * 2;  // bytes per lane load
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_cache) |
+         reinterpret_cast<uintptr_t>(v_cache)) % vec != 0)
+      return set_error(FD_ERR_UNSUPPORTED, "q/k/v not aligned to %d bytes", vec);
+    const cudaError_t e = fd::launch_decode_simt(sp, dtype, out_fp32, st);
+    if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "simt launch: %s", cudaGetErrorString(e));
+    return set_ok();
+  }
+
+  const int sms = device_sms(dev);
+  if (sms <= 0) return set_error(FD_ERR_CUDA, "cannot query SM count");
+  const int64_t nb_max = batch_size < fd::kMaxBatchPerLaunch ? batch_size : fd::kMaxBatchPerLaunch;
+  const fd::WorkspaceLayout wl = fd::workspace_layout(nb_max, num_heads_k, group, sms);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (ws == nullptr) {
+    ws = static_cast<uint8_t*>(internal_workspace(dev, wl.total, st));
+    if (ws == nullptr) return set_error(FD_ERR_WORKSPACE, "cannot allocate %zu-byte workspace", wl.total);
+  } else if (workspace_bytes < wl.total) {
+    return set_error(FD_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes,
+                     wl.total);
+  } else if (!aligned16(ws)) {
+    return set_error(FD_ERR_WORKSPACE, "workspace not 16-byte aligned");
+  }
+
+  const int es = esize(dtype);
+  const int64_t kv_max = block_table_stride * page_block_size;
+  const int64_t len_bound =
+      max_seqlen_k > 0 ? (max_seqlen_k < kv_max ? max_seqlen_k : kv_max) : kv_max;
+  const int64_t tiles_bound = len_bound > 0 ? (len_bound + fd::kTileTokens - 1) / fd::kTileTokens : 1;
+
+  CUtensorMap tm_k, tm_v;
+  {
+    const cuuint64_t dims[4] = {128, (cuuint64_t)num_heads_k, (cuuint64_t)page_block_size,
+                                (cuuint64_t)num_blocks};
+    const cuuint64_t strides[3] = {(cuuint64_t)(128 * es), (cuuint64_t)(num_heads_k * 128 * es),
+                                   (cuuint64_t)(page_block_size * num_heads_k * 128 * es)};
+    const cuuint32_t box[4] = {64, 1, (cuuint32_t)chunk, 1};
+    CUresult r = encode(&tm_k, dtype, 4, k_cache, dims, strides, box);
+    if (r == CUDA_SUCCESS) r = encode(&tm_v, dtype, 4, v_cache, dims, strides, box);
+    if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "K/V tensor map encode failed (%d)", (int)r);
+  }
+
+  for (int64_t b0 = 0; b0 < batch_size; b0 += fd::kMaxBatchPerLaunch) {
+    const int64_t nb = batch_size - b0 < fd::kMaxBatchPerLaunch ? batch_size - b0
+                                                                 : fd::kMaxBatchPerLaunch;
+    CUtensorMap tm_q;
+    {
+      const uint8_t* qb = static_cast<const uint8_t*>(q) + b0 * num_heads * 128 * es;
+      const cuuint64_t dims[3] = {128, (cuuint64_t)num_heads, (cuuint64_t)nb};
+      const cuuint64_t strides[2] = {(cuuint64_t)(128 * es), (cuuint64_t)(num_heads * 128 * es)};
+      const cuuint32_t box[3] = {64, (cuuint32_t)group, 1};
+      const CUresult r = encode(&tm_q, dtype, 3, qb, dims, strides, box);
+      if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "Q tensor map encode failed (%d)", (int)r);
+    }
+    fd::DecodeParams p;
+    p.out = static_cast<uint8_t*>(out) + b0 * num_heads * 128 * esize(out_dtype);
+    p.lse = lse != nullptr ? lse + b0 * num_heads : nullptr;
+    p.seqlens = cache_seqlens + b0;
+    p.block_table = block_table + b0 * block_table_stride;
+    p.bt_stride = block_table_stride;
+    p.batch = static_cast<int>(nb);
+    p.num_heads = static_cast<int>(num_heads);
+    p.num_heads_k = static_cast<int>(num_heads_k);
+    p.group = group;
+    p.page = static_cast<int>(page_block_size);
+    p.chunk = chunk;
+    p.scale_log2 = scale_log2;
+    p.err = reinterpret_cast<int*>(ws + wl.err_off);
+    p.tickets = reinterpret_cast<uint32_t*>(ws + wl.tickets_off);
+    p.part_lse = reinterpret_cast<float*>(ws + wl.lse_off);
+    p.part_o = reinterpret_cast<float*>(ws + wl.o_off);
+    p.timeout_ns = timeout_ns();
+    const int64_t work_bound = nb * num_heads_k * tiles_bound;
+    const int grid = static_cast<int>(work_bound < sms ? work_bound : sms);
+    const cudaError_t e = fd::launch_decode_sm100(tm_q, tm_k, tm_v, p, dtype, out_fp32, grid, st);
+    if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "sm100 launch: %s", cudaGetErrorString(e));
+  }
+  return set_ok();
+}
+
+void run_kernel(const void* q, const void* k_cache_paged, const void* v_cache_paged, void* output,
+                const int32_t* cache_seqlens, const int32_t* block_table, int64_t batch_size,
+                int64_t seqlen_k, int64_t seqlen_q, int64_t num_heads, int64_t num_heads_k,
+                int64_t headdim, int64_t page_block_size, int64_t num_blocks, int64_t causal) {
+  (void)causal;  // one query token: the causal mask admits every cached key
+  if (seqlen_q != 1) {
+    set_error(FD_ERR_UNSUPPORTED, "seqlen_q=%lld: only single-token decode", (long long)seqlen_q);
+    return;
+  }
+  if (batch_size <= 0 || num_blocks <= 0 || headdim <= 0) {
+    set_error(FD_ERR_INVALID_ARG, "batch_size, num_blocks and headdim must be positive");
+    return;
+  }
+  const int64_t bt_stride = num_blocks / batch_size;  // reference: blocks_per_batch
+  if (bt_stride <= 0) {
+    set_error(FD_ERR_INVALID_ARG, "num_blocks %lld < batch_size %lld", (long long)num_blocks,
+              (long long)batch_size);
+    return;
+  }
+  const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(headdim)));
+  fd_decode_paged(q, k_cache_paged, v_cache_paged, output, nullptr, cache_seqlens, block_table,
+                  bt_stride, batch_size, num_heads, num_heads_k, headdim, page_block_size,
+                  num_blocks, FD_DTYPE_BF16, FD_DTYPE_BF16, scale, seqlen_k, nullptr, 0, nullptr);
+}
+
+int fd_combine_lse(const float* part_o, const float* part_lse, int64_t n_parts, int64_t rows,
+                   int64_t headdim, void* out, int out_dtype, float* lse_out, void* stream) {
+  if (part_o == nullptr || part_lse == nullptr || out == nullptr)
+    return set_error(FD_ERR_INVALID_ARG, "null pointer");
+  if (n_parts <= 0 || rows < 0 || headdim <= 0 || rows > INT32_MAX)
+    return set_error(FD_ERR_INVALID_ARG, "bad sizes");
+  if (out_dtype != FD_DTYPE_BF16 && out_dtype != FD_DTYPE_FP16 && out_dtype != FD_DTYPE_FP32)
+    return set_error(FD_ERR_INVALID_ARG, "bad out_dtype");
+  const cudaError_t e = fd::launch_combine_lse(part_o, part_lse, n_parts, rows, headdim, out,
+                                               out_dtype, lse_out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "combine launch: %s", cudaGetErrorString(e));
+  return set_ok();
+}
+
+int fd_selftest_bounded_wait(uint64_t budget_ns, uint64_t* waited_ns) {
+  int* d_status = nullptr;
+  unsigned long long* d_waited = nullptr;
+  if (cudaMalloc(&d_status, sizeof(int)) != cudaSuccess)
+    return set_error(FD_ERR_CUDA, "cudaMalloc failed");
+  if (cudaMalloc(&d_waited, sizeof(unsigned long long)) != cudaSuccess) {
+    cudaFree(d_status);
+    return set_error(FD_ERR_CUDA, "cudaMalloc failed");
+  }
+  int status = -1;
+  unsigned long long waited = 0;
+  cudaError_t e = fd::launch_bounded_wait_probe(budget_ns, d_status, d_waited, nullptr);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(&status, d_status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(&waited, d_waited, sizeof(waited), cudaMemcpyDeviceToHost);
+  cudaFree(d_status);
+  cudaFree(d_waited);
+  if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "probe: %s", cudaGetErrorString(e));
+  if (waited_ns != nullptr) *waited_ns = waited;
+  if (status == FD_ERR_DEVICE_TIMEOUT)
+    return set_error(FD_ERR_DEVICE_TIMEOUT, "bounded wait gave up after %llu ns", waited);
+  return set_ok();
+}
+
+int fd_device_status(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices)
+    return set_error(FD_ERR_CUDA, "no current CUDA device");
+  if (cudaDeviceSynchronize() != cudaSuccess)
+    return set_error(FD_ERR_CUDA, "device synchronize failed");
+  void* ws = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_dev[dev].mu);
+    ws = g_dev[dev].ws;
+  }
+  if (ws == nullptr) return set_ok();
+  int word = 0;
+  if (cudaMemcpy(&word, ws, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return set_error(FD_ERR_CUDA, "cannot read device status");
+  if (word != 0) {
+    const int zero = 0;
+    cudaMemcpy(ws, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    return set_error(FD_ERR_DEVICE_TIMEOUT, "device reported status %d", word);
+  }
+  return set_ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,640 @@
+// fd_decode_sm100.cu - persistent split-KV paged decode kernel for B200.
+//
+// Work decomposition (replaces the reference's fixed split table and
+// per-split grid, submission-oj/best_flashattn_kvcache_decode.cu:1039-1076,
+// :1381-1418, and its balanced page ranges :664-671): every (sequence b,
+// KV head) pair is a row of 128-token tiles; the rows are laid end to end
+// (b-major, then KV head) and the resulting line of W tiles is cut into
+// gridDim.x equal contiguous ranges, one per persistent CTA.  A CTA walks
+// its range segment by segment (a segment = the part of one pair inside the
+// range).  A pair that lies inside one CTA is written straight to the
+// output; a pair cut by range boundaries leaves one normalised partial
+// (O, log2-LSE) per segment and the CTA that finishes last merges them
+// (replaces the separate combine launch, best :956-1037, :1420-1425).
+//
+// Per tile the CTA runs, warp-specialised:
+//   warp 0    TMA producer: gathers the tile's K and V rows page by page
+//             through block_table into a 3-deep shared-memory ring
+//             (128B-swizzled, two 64-dim halves), and the group's query rows.
+//   warp 1    tcgen05 issuer: S^T[tok, head] = K . Q^T (M=128 tokens, N=16
+//             heads, K=128 dims) into TMEM, then O^T[dim, head] = V^T . P^T
+//             (M=128 dims, N=16 heads, K=128 tokens) into TMEM.
+//   warps 2-5 softmax + epilogue: thread = TMEM lane = token row for S and
+//             head-dim for O; fp32 online softmax in the log2 domain (the
+//             reference's convention, best :541-578), P written to shared
+//             memory for the second UMMA, per-tile O folded into registers.
+// One KV byte is read from HBM exactly once; the arithmetic runs on the
+// tensor cores so the SM's issue slots stay free for the memory pipeline.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "fd_kernels.h"
+#include "fd_ptx.cuh"
+
+namespace fd {
+
+namespace {
+
+constexpr int kStages = 3;
+constexpr int kHalfBytes = kTileTokens * 128;    // 128 tokens x 64 dims x 2 B = 16 KB
+constexpr int kOperandBytes = 2 * kHalfBytes;    // one K or V tile: 32 KB
+constexpr int kStageBytes = 2 * kOperandBytes;   // K + V: 64 KB
+constexpr int kQSlotBytes = 2 * kMaxGroup * 128; // two halves x 16 rows x 128 B
+constexpr int kPBufBytes = kTileTokens * kMaxGroup * 2;  // 128 tokens x 16 heads x 2 B
+constexpr int kTmemCols = 64;                    // S0 S1 O0 O1, 16 columns each
+constexpr int kNumBars = 2 * kStages + 14;
+
+// Shared-memory carve-up, offsets from a 1024-byte aligned base.
+constexpr int kOffStages = 0;
+constexpr int kOffQ = kOffStages + kStages * kStageBytes;
+constexpr int kOffP = kOffQ + 2 * kQSlotBytes;
+constexpr int kOffBars = kOffP + 2 * kPBufBytes;
+constexpr int kOffMisc = kOffBars + kNumBars * 8;            // tmem slot, abort, last flag
+constexpr int kOffRed = (kOffMisc + 64 + 15) & ~15;          // [2][4][16] floats tile maxima
+constexpr int kOffFin = kOffRed + 2 * 4 * kMaxGroup * 4;     // [4][16] floats row sums
+constexpr int kOffPrefix = kOffFin + 4 * kMaxGroup * 4;      // [B+1] ints tile prefix sums
+constexpr int kSmemUsed = kOffPrefix + (kMaxBatchPerLaunch + 1) * 4;
+constexpr int kSmemBytes = kSmemUsed + 1024;                 // slack for 1024-B alignment
+static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
+
+// TMEM columns: S^T of tile parity b at 16*b, O^T of tile parity b at 32+16*b.
+__device__ __forceinline__ uint32_t col_s(int b) { return static_cast<uint32_t>(b) * 16u; }
+__device__ __forceinline__ uint32_t col_o(int b) { return 32u + static_cast<uint32_t>(b) * 16u; }
+
+// UMMA shared-memory descriptor (tcgen05 matrix descriptor): start address,
+// leading/stride byte offsets (16-byte units), version 1, layout type.
+__device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                               uint32_t layout) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;
+  d |= static_cast<uint64_t>(layout) << 61;
+  return d;
+}
+constexpr uint32_t kLayoutNone = 0;
+constexpr uint32_t kLayoutSw128 = 2;
+
+// UMMA instruction descriptor for kind::f16 with an fp32 accumulator.
+__host__ __device__ constexpr uint32_t make_idesc(bool bf16, bool a_mn_major, bool b_mn_major,
+                                                  int m, int n) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
+         ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+template <typename T> struct DType;
+template <> struct DType<__nv_bfloat16> {
+  static constexpr bool kBf16 = true;
+  static __device__ __forceinline__ uint32_t pack2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+template <> struct DType<__half> {
+  static constexpr bool kBf16 = false;
+  static __device__ __forceinline__ uint32_t pack2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+
+template <typename O> __device__ __forceinline__ O to_out(float x);
+template <> __device__ __forceinline__ float to_out<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 to_out<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+template <> __device__ __forceinline__ __half to_out<__half>(float x) { return __float2half_rn(x); }
+
+// One segment of a CTA's tile range: the tiles of pair (b, kvh) that fall in
+// [w, min(range_end, pair_end)).
+struct Segment {
+  int b, kvh, pair;
+  int tile0, ntiles;
+  int seqlen;
+  int nseg, cfirst;  // how many CTAs share this pair, and the first of them
+};
+
+__device__ __forceinline__ int64_t cta_of(int64_t w, int64_t total, int grid) {
+  // largest c with floor(total * c / grid) <= w
+  return ((w + 1) * grid + total - 1) / total - 1;
+}
+
+__device__ __forceinline__ Segment locate(const int* __restrict__ prefix, int batch, int hkv,
+                                          int64_t total, int grid, int64_t w, int64_t range_end,
+                                          const int32_t* __restrict__ seqlens, int64_t max_len) {
+  int lo = 0, hi = batch - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (static_cast<int64_t>(hkv) * prefix[mid] <= w) lo = mid; else hi = mid - 1;
+  }
+  Segment s;
+  s.b = lo;
+  const int n = prefix[lo + 1] - prefix[lo];
+  const int64_t r = w - static_cast<int64_t>(hkv) * prefix[lo];
+  s.kvh = static_cast<int>(r / n);
+  s.tile0 = static_cast<int>(r - static_cast<int64_t>(s.kvh) * n);
+  s.pair = lo * hkv + s.kvh;
+  const int64_t pair_start = w - s.tile0;
+  const int64_t pair_end = pair_start + n;
+  const int64_t seg_end = range_end < pair_end ? range_end : pair_end;
+  s.ntiles = static_cast<int>(seg_end - w);
+  int len = __ldg(seqlens + lo);
+  len = len < 0 ? 0 : len;
+  s.seqlen = static_cast<int>(len > max_len ? max_len : len);
+  const int64_t c0 = cta_of(pair_start, total, grid);
+  const int64_t c1 = cta_of(pair_end - 1, total, grid);
+  s.cfirst = static_cast<int>(c0);
+  s.nseg = static_cast<int>(c1 - c0 + 1);
+  return s;
+}
+
+__device__ __forceinline__ bool lane0_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                           uint64_t budget, int lane) {
+  int ok = 1;
+  if (lane == 0) ok = mbar_wait_bounded(bar, parity, abort_flag, budget) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+template <typename T, typename OutT, int NCOL>
+__global__ void __launch_bounds__(kSm100Threads, 1)
+    decode_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
+                        const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const DecodeParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+
+  uint8_t* stages = smem + kOffStages;
+  uint8_t* qslots = smem + kOffQ;
+  uint8_t* pbufs = smem + kOffP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kStages;
+  uint64_t* q_full = bars + 2 * kStages;
+  uint64_t* q_empty = q_full + 2;
+  uint64_t* s_full = q_empty + 2;
+  uint64_t* s_empty = s_full + 2;
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* o_full = p_full + 2;
+  uint64_t* o_empty = o_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 8);
+  float* red = reinterpret_cast<float*>(smem + kOffRed);
+  float* fin = reinterpret_cast<float*>(smem + kOffFin);
+  int* prefix = reinterpret_cast<int*>(smem + kOffPrefix);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int batch = p.batch;
+  const int hkv = p.num_heads_k;
+  const int group = p.group;
+  const uint64_t budget = p.timeout_ns;
+  const int64_t max_len = p.bt_stride * static_cast<int64_t>(p.page);
+
+  // ------------------------------------------------------------ prologue
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], 128);
+    }
+    *abort_flag = 0;
+    *last_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  // Zero the query slots (rows >= group stay zero) and the P buffers
+  // (heads >= group stay zero): 16 KB.
+  {
+    uint4* z = reinterpret_cast<uint4*>(qslots);
+    const int n16 = (2 * kQSlotBytes + 2 * kPBufBytes) / 16;
+    for (int i = tid; i < n16; i += kSm100Threads) z[i] = make_uint4(0, 0, 0, 0);
+  }
+  for (int b = tid; b < batch; b += kSm100Threads) {
+    int len = __ldg(p.seqlens + b);
+    len = len < 0 ? 0 : len;
+    const int64_t l64 = len > max_len ? max_len : len;
+    prefix[b + 1] = l64 > 0 ? static_cast<int>((l64 + kTileTokens - 1) / kTileTokens) : 1;
+  }
+  if (tid == 0) prefix[0] = 0;
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) {  // inclusive scan of tile counts -> exclusive prefix sums
+    int carry = 0;
+    for (int base = 1; base <= batch; base += 32) {
+      const int idx = base + lane;
+      int v = idx <= batch ? prefix[idx] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+      }
+      v += carry;
+      if (idx <= batch) prefix[idx] = v;
+      carry = __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
+  __syncthreads();
+
+  const uint32_t tmem = *tmem_slot;
+  const int grid = gridDim.x;
+  const int cta = blockIdx.x;
+  const int64_t total = static_cast<int64_t>(hkv) * prefix[batch];
+  const int64_t w_begin = total * cta / grid;
+  const int64_t w_end = total * (cta + 1) / grid;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+    }
+    const uint64_t pol_stream = policy_evict_first();
+    const uint64_t pol_keep = policy_evict_last();
+    const int chunk = p.chunk;  // tokens per TMA box; never crosses a page
+    const int nchunks = kTileTokens / chunk;
+    int64_t it = 0;
+    int sc = 0;
+    bool ok = true;
+    for (int64_t w = w_begin; w < w_end && ok; ++sc) {
+      const Segment s = locate(prefix, batch, hkv, total, grid, w, w_end, p.seqlens, max_len);
+      const int qs = sc & 1;
+      ok = lane0_wait(&q_empty[qs], ((sc >> 1) & 1) ^ 1, abort_flag, budget, lane);
+      if (!ok) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&q_full[qs], 2u * group * 128u);
+        uint8_t* dst = qslots + qs * kQSlotBytes;
+        tma_load_3d(&tm_q, &q_full[qs], dst, 0, s.kvh * group, s.b, pol_keep);
+        tma_load_3d(&tm_q, &q_full[qs], dst + kQSlotBytes / 2, 64, s.kvh * group, s.b, pol_keep);
+      }
+      const int32_t* bt_row = p.block_table + static_cast<int64_t>(s.b) * p.bt_stride;
+      for (int t = 0; t < s.ntiles; ++t, ++it) {
+        const int tok0 = (s.tile0 + t) * kTileTokens;
+        const int pos = tok0 + lane * chunk;
+        const bool need = lane < nchunks && pos < s.seqlen;
+        int page_id = 0;
+        if (need) page_id = __ldg(bt_row + pos / p.page);  // issued before the wait
+        const uint32_t nneed = __popc(__ballot_sync(0xffffffffu, need));
+        const int stage = static_cast<int>(it % kStages);
+        ok = lane0_wait(&empty[stage], static_cast<uint32_t>((it / kStages) & 1) ^ 1u, abort_flag,
+                        budget, lane);
+        if (!ok) break;
+        if (lane == 0) mbar_arrive_expect_tx(&full[stage], nneed * static_cast<uint32_t>(chunk) * 512u);
+        __syncwarp();
+        if (need) {
+          const int off = pos % p.page;
+          uint8_t* kdst = stages + stage * kStageBytes + lane * chunk * 128;
+          uint8_t* vdst = kdst + kOperandBytes;
+          tma_load_4d(&tm_k, &full[stage], kdst, 0, s.kvh, off, page_id, pol_stream);
+          tma_load_4d(&tm_k, &full[stage], kdst + kHalfBytes, 64, s.kvh, off, page_id, pol_stream);
+          tma_load_4d(&tm_v, &full[stage], vdst, 0, s.kvh, off, page_id, pol_stream);
+          tma_load_4d(&tm_v, &full[stage], vdst + kHalfBytes, 64, s.kvh, off, page_id, pol_stream);
+        }
+        __syncwarp();
+      }
+      w += s.ntiles;
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- UMMA issuer
+    constexpr bool kBf16 = DType<T>::kBf16;
+    constexpr uint32_t idesc_qk = make_idesc(kBf16, false, false, 128, kMaxGroup);
+    constexpr uint32_t idesc_pv = make_idesc(kBf16, true, true, 128, kMaxGroup);
+    int64_t it = 0;
+    int sc = 0;
+    bool ok = true;
+    auto issue_pv = [&](int64_t i) -> bool {
+      const int pb = static_cast<int>(i & 1);
+      const uint32_t ph = static_cast<uint32_t>((i >> 1) & 1);
+      const int stage = static_cast<int>(i % kStages);
+      if (!lane0_wait(&p_full[pb], ph, abort_flag, budget, lane)) return false;
+      if (!lane0_wait(&o_empty[pb], ph ^ 1u, abort_flag, budget, lane)) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t vaddr = smem_u32(stages + stage * kStageBytes + kOperandBytes);
+        const uint32_t paddr = smem_u32(pbufs + pb * kPBufBytes);
+#pragma unroll
+        for (int j = 0; j < kTileTokens / 16; ++j) {
+          // A = V^T: MN-major (head-dim contiguous), 128B swizzle; the two
+          // 64-dim halves are 16 KB apart (LBO), 8-token groups 1 KB apart (SBO).
+          const uint64_t a = make_sdesc(vaddr + j * 2048, kHalfBytes, 1024, kLayoutSw128);
+          // B = P^T: MN-major (heads contiguous), no swizzle; 8-head core
+          // matrices 128 B apart (SBO), 8-token groups 256 B apart (LBO).
+          const uint64_t b = make_sdesc(paddr + j * 512, 256, 128, kLayoutNone);
+          umma_f16(tmem + col_o(pb), a, b, idesc_pv, j > 0 ? 1u : 0u);
+        }
+        umma_commit(&o_full[pb]);
+        umma_commit(&empty[stage]);
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int64_t w = w_begin; w < w_end && ok; ++sc) {
+      const Segment s = locate(prefix, batch, hkv, total, grid, w, w_end, p.seqlens, max_len);
+      const int qs = sc & 1;
+      ok = lane0_wait(&q_full[qs], (sc >> 1) & 1, abort_flag, budget, lane);
+      if (!ok) break;
+      for (int t = 0; t < s.ntiles; ++t, ++it) {
+        const int stage = static_cast<int>(it % kStages);
+        const int sb = static_cast<int>(it & 1);
+        ok = lane0_wait(&full[stage], static_cast<uint32_t>((it / kStages) & 1), abort_flag, budget,
+                        lane);
+        if (ok) ok = lane0_wait(&s_empty[sb], static_cast<uint32_t>(((it >> 1) & 1) ^ 1), abort_flag,
+                                budget, lane);
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t kaddr = smem_u32(stages + stage * kStageBytes);
+          const uint32_t qaddr = smem_u32(qslots + qs * kQSlotBytes);
+#pragma unroll
+          for (int j = 0; j < kHeadDim / 16; ++j) {
+            // A = K tile, K-major 128B swizzle: 8-row groups 1 KB apart; the
+            // 16-dim step j moves 32 B inside a 128 B row, 64-dim halves 16 KB apart.
+            const uint64_t a =
+                make_sdesc(kaddr + (j >> 2) * kHalfBytes + (j & 3) * 32, 16, 1024, kLayoutSw128);
+            const uint64_t b = make_sdesc(qaddr + (j >> 2) * (kQSlotBytes / 2) + (j & 3) * 32, 16,
+                                          1024, kLayoutSw128);
+            umma_f16(tmem + col_s(sb), a, b, idesc_qk, j > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[sb]);
+          if (t == s.ntiles - 1) umma_commit(&q_empty[qs]);
+        }
+        __syncwarp();
+        if (it > 0) {
+          ok = issue_pv(it - 1);
+          if (!ok) break;
+        }
+      }
+      w += s.ntiles;
+    }
+    if (ok && it > 0) issue_pv(it - 1);
+  } else {
+    // ---------------------------------------------------------- softmax warps
+    const int quad = warp & 3;      // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;  // token row of S, head-dim index of O
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const float neg_inf = -__int_as_float(0x7f800000);
+    const int hq = p.num_heads;
+    OutT* out = reinterpret_cast<OutT*>(p.out);
+    int64_t it = 0;
+    for (int64_t w = w_begin; w < w_end;) {
+      const Segment s = locate(prefix, batch, hkv, total, grid, w, w_end, p.seqlens, max_len);
+      float m_run[NCOL], l_run[NCOL], o_acc[NCOL], a_prev[NCOL];
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) {
+        m_run[h] = neg_inf;
+        l_run[h] = 0.f;
+        o_acc[h] = 0.f;
+        a_prev[h] = 0.f;
+      }
+      auto consume_o = [&](int64_t i) {
+        const int pb = static_cast<int>(i & 1);
+        mbar_wait_bounded(&o_full[pb], static_cast<uint32_t>((i >> 1) & 1), abort_flag, budget);
+        tc_fence_after();
+        uint32_t r[NCOL];
+        if constexpr (NCOL == 8) tmem_ld_x8(lane_addr + col_o(pb), r); else tmem_ld_x16(lane_addr + col_o(pb), r);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&o_empty[pb]);
+#pragma unroll
+        for (int h = 0; h < NCOL; ++h) o_acc[h] = fmaf(o_acc[h], a_prev[h], __uint_as_float(r[h]));
+      };
+      for (int t = 0; t < s.ntiles; ++t, ++it) {
+        const int sb = static_cast<int>(it & 1);
+        const int stage = static_cast<int>(it % kStages);
+        mbar_wait_bounded(&s_full[sb], static_cast<uint32_t>((it >> 1) & 1), abort_flag, budget);
+        tc_fence_after();
+        uint32_t r[NCOL];
+        if constexpr (NCOL == 8) tmem_ld_x8(lane_addr + col_s(sb), r); else tmem_ld_x16(lane_addr + col_s(sb), r);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&s_empty[sb]);
+
+        const int tok0 = (s.tile0 + t) * kTileTokens;
+        const int valid_rows = s.seqlen - tok0;  // may exceed 128; <=0 only for empty sequences
+        const bool valid = row < valid_rows;
+        float sv[NCOL];
+        float* red_t = red + (it & 1) * (4 * kMaxGroup);
+#pragma unroll
+        for (int h = 0; h < NCOL; ++h) {
+          sv[h] = valid ? __uint_as_float(r[h]) * p.scale_log2 : neg_inf;
+          const float wm = warp_max_f32(sv[h]);
+          if (lane == 0) red_t[quad * kMaxGroup + h] = wm;
+        }
+        named_bar_sync(1, 128);
+        float pv[NCOL];
+#pragma unroll
+        for (int h = 0; h < NCOL; ++h) {
+          const float tmax = fmaxf(fmaxf(red_t[h], red_t[kMaxGroup + h]),
+                                   fmaxf(red_t[2 * kMaxGroup + h], red_t[3 * kMaxGroup + h]));
+          const float m_new = fmaxf(m_run[h], tmax);
+          const float m_use = m_new == neg_inf ? 0.f : m_new;
+          const float alpha = fast_exp2(m_run[h] - m_use);
+          const float pe = (h < group) ? fast_exp2(sv[h] - m_use) : 0.f;
+          l_run[h] = fmaf(l_run[h], alpha, pe);
+          m_run[h] = m_new;
+          pv[h] = pe;
+          sv[h] = alpha;  // keep this tile's rescale factor
+        }
+        if (valid_rows < kTileTokens && !valid) {
+          // Rows past the sequence end: stale or never-written data must not
+          // reach P.V (0 * NaN), so zero this token's V row in the stage.
+          uint4* vrow0 = reinterpret_cast<uint4*>(stages + stage * kStageBytes + kOperandBytes + row * 128);
+          uint4* vrow1 = reinterpret_cast<uint4*>(stages + stage * kStageBytes + kOperandBytes + kHalfBytes + row * 128);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            vrow0[i] = make_uint4(0, 0, 0, 0);
+            vrow1[i] = make_uint4(0, 0, 0, 0);
+          }
+        }
+        {
+          uint8_t* prow = pbufs + sb * kPBufBytes + (row >> 3) * 256 + (row & 7) * 16;
+          uint4 lo;
+          lo.x = DType<T>::pack2(pv[0], pv[1]);
+          lo.y = DType<T>::pack2(pv[2], pv[3]);
+          lo.z = DType<T>::pack2(pv[4], pv[5]);
+          lo.w = DType<T>::pack2(pv[6], pv[7]);
+          *reinterpret_cast<uint4*>(prow) = lo;
+          if constexpr (NCOL == 16) {
+            uint4 hi;
+            hi.x = DType<T>::pack2(pv[8], pv[9]);
+            hi.y = DType<T>::pack2(pv[10], pv[11]);
+            hi.z = DType<T>::pack2(pv[12], pv[13]);
+            hi.w = DType<T>::pack2(pv[14], pv[15]);
+            *reinterpret_cast<uint4*>(prow + 128) = hi;
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&p_full[sb]);
+        if (t > 0) consume_o(it - 1);
+#pragma unroll
+        for (int h = 0; h < NCOL; ++h) a_prev[h] = sv[h];
+      }
+      consume_o(it - 1);
+
+      // ---- segment epilogue: row sums across the 128 threads
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) {
+        float v = l_run[h];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) fin[quad * kMaxGroup + h] = v;
+      }
+      named_bar_sync(1, 128);
+      float l_tot[NCOL];
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h)
+        l_tot[h] = (fin[h] + fin[kMaxGroup + h]) + (fin[2 * kMaxGroup + h] + fin[3 * kMaxGroup + h]);
+      const int d = row;
+      if (s.nseg == 1) {
+        const int64_t obase = (static_cast<int64_t>(s.b) * hq + s.kvh * group) * kHeadDim + d;
+#pragma unroll
+        for (int h = 0; h < NCOL; ++h) {
+          if (h < group) {
+            const float v = l_tot[h] > 0.f ? o_acc[h] / l_tot[h] : 0.f;
+            out[obase + static_cast<int64_t>(h) * kHeadDim] = to_out<OutT>(v);
+            if (p.lse != nullptr && d == h) {
+              p.lse[static_cast<int64_t>(s.b) * hq + s.kvh * group + h] =
+                  l_tot[h] > 0.f ? (m_run[h] + fast_log2(l_tot[h])) * 0.69314718055994531f : neg_inf;
+            }
+          }
+        }
+      } else {
+        const int64_t slot = static_cast<int64_t>(cta) + s.pair;
+        float* po = p.part_o + slot * group * kHeadDim + d;
+#pragma unroll
+        for (int h = 0; h < NCOL; ++h) {
+          if (h < group) {
+            po[h * kHeadDim] = l_tot[h] > 0.f ? o_acc[h] / l_tot[h] : 0.f;
+            if (d == h) p.part_lse[slot * group + h] = l_tot[h] > 0.f ? m_run[h] + fast_log2(l_tot[h]) : neg_inf;
+          }
+        }
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (d == 0) {
+          int is_last = 0;
+          if (!*abort_flag) {
+            const unsigned old = atomicInc(p.tickets + s.pair, static_cast<unsigned>(s.nseg - 1));
+            is_last = old == static_cast<unsigned>(s.nseg - 1);
+          }
+          *last_flag = is_last;
+        }
+        named_bar_sync(1, 128);
+        if (*last_flag) {
+          __threadfence();
+          const int64_t sbase = static_cast<int64_t>(s.cfirst) + s.pair;
+          for (int h = 0; h < group; ++h) {
+            float mx = neg_inf;
+            for (int j = 0; j < s.nseg; ++j) mx = fmaxf(mx, __ldcg(p.part_lse + (sbase + j) * group + h));
+            float den = 0.f, acc = 0.f;
+            for (int j = 0; j < s.nseg; ++j) {
+              const float lj = __ldcg(p.part_lse + (sbase + j) * group + h);
+              const float wj = lj == neg_inf ? 0.f : fast_exp2(lj - mx);
+              if (wj > 0.f) {
+                acc = fmaf(wj, __ldcg(p.part_o + ((sbase + j) * group + h) * kHeadDim + d), acc);
+                den += wj;
+              }
+            }
+            const int64_t oidx = (static_cast<int64_t>(s.b) * hq + s.kvh * group + h) * kHeadDim + d;
+            out[oidx] = to_out<OutT>(den > 0.f ? acc / den : 0.f);
+            if (p.lse != nullptr && d == 0)
+              p.lse[static_cast<int64_t>(s.b) * hq + s.kvh * group + h] =
+                  den > 0.f ? (mx + fast_log2(den)) * 0.69314718055994531f : neg_inf;
+          }
+        }
+      }
+      named_bar_sync(1, 128);  // fin / last_flag are reused by the next segment
+      w += s.ntiles;
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) {
+    if (tid == 0) {
+      atomicExch(p.err, 5);
+      // Let any copy or MMA still in flight land before the CTA's shared
+      // memory and TMEM are released (bounded: 2 ms).
+      const uint64_t t0 = globaltimer_ns();
+      while (globaltimer_ns() - t0 < 2000000ull) {
+      }
+    }
+    __syncthreads();
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <typename T, typename OutT, int NCOL>
+cudaError_t launch_typed(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                         const DecodeParams& p, int grid, cudaStream_t stream) {
+  auto kern = decode_sm100_kernel<T, OutT, NCOL>;
+  // The attribute is per device; setting it again is harmless.
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if ((__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & bit) == 0) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
+  }
+  kern<<<grid, kSm100Threads, kSmemBytes, stream>>>(tm_q, tm_k, tm_v, p);
+  return cudaGetLastError();
+}
+
+template <typename T, typename OutT>
+cudaError_t launch_ncol(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                        const DecodeParams& p, int grid, cudaStream_t stream) {
+  if (p.group <= 8) return launch_typed<T, OutT, 8>(tm_q, tm_k, tm_v, p, grid, stream);
+  return launch_typed<T, OutT, 16>(tm_q, tm_k, tm_v, p, grid, stream);
+}
+
+}  // namespace
+
+size_t sm100_smem_bytes() { return static_cast<size_t>(kSmemBytes); }
+
+WorkspaceLayout workspace_layout(int64_t batch_per_launch, int64_t num_heads_k, int64_t group,
+                                 int grid_max) {
+  auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  const size_t pairs = static_cast<size_t>(batch_per_launch * num_heads_k);
+  const size_t slots = pairs + static_cast<size_t>(grid_max);
+  WorkspaceLayout w;
+  w.err_off = 0;
+  w.tickets_off = 256;
+  w.lse_off = w.tickets_off + up(pairs * 4);
+  w.o_off = w.lse_off + up(slots * group * 4);
+  w.total = w.o_off + up(slots * group * kHeadDim * 4);
+  return w;
+}
+
+cudaError_t launch_decode_sm100(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                                const CUtensorMap& tm_v, const DecodeParams& p, int dtype,
+                                bool out_fp32, int grid, cudaStream_t stream) {
+  if (dtype == 0) {
+    return out_fp32 ? launch_ncol<__nv_bfloat16, float>(tm_q, tm_k, tm_v, p, grid, stream)
+                    : launch_ncol<__nv_bfloat16, __nv_bfloat16>(tm_q, tm_k, tm_v, p, grid, stream);
+  }
+  return out_fp32 ? launch_ncol<__half, float>(tm_q, tm_k, tm_v, p, grid, stream)
+                  : launch_ncol<__half, __half>(tm_q, tm_k, tm_v, p, grid, stream);
+}
+
+}  // namespace fd

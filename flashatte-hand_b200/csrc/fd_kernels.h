@@ -1,0 +1,65 @@
+// fd_kernels.h - host-visible launch interface of the device kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace fd {
+
+constexpr int kHeadDim = 128;          // head dim of the tensor-core path
+constexpr int kTileTokens = 128;       // KV tokens per pipeline stage (UMMA M of Q.K^T)
+constexpr int kMaxGroup = 16;          // query heads per KV head (UMMA N, padded)
+constexpr int kMaxBatchPerLaunch = 2048;  // sequences per launch (schedule lives in smem)
+constexpr int kSm100Threads = 192;     // warp0 TMA, warp1 MMA, warps2-5 softmax/epilogue
+
+// Per-launch parameters of the tensor-core kernel (tensor maps travel as
+// separate __grid_constant__ arguments).
+struct DecodeParams {
+  void* out;                  // [B, Hq, 128] of OutT
+  float* lse;                 // [B, Hq] natural log, nullable
+  const int32_t* seqlens;     // [B]
+  const int32_t* block_table; // [B, bt_stride]
+  int64_t bt_stride;
+  int batch, num_heads, num_heads_k, group, page, chunk;
+  float scale_log2;           // softmax_scale * log2(e)
+  float* part_o;              // [slots, group, 128] fp32 (normalised partial O)
+  float* part_lse;            // [slots, group] log2-domain partial LSE
+  uint32_t* tickets;          // [batch * num_heads_k] arrival counters, zero at rest
+  int* err;                   // device error word
+  unsigned long long timeout_ns;
+};
+
+struct SimtParams {
+  const void* q; const void* k; const void* v;
+  void* out; float* lse;
+  const int32_t* seqlens; const int32_t* block_table;
+  int64_t bt_stride;
+  int batch, num_heads, num_heads_k, group, head_dim, page;
+  int64_t num_blocks;
+  float scale_log2;
+};
+
+// Workspace carve-up for the tensor-core kernel.
+struct WorkspaceLayout {
+  size_t err_off, tickets_off, lse_off, o_off, total;
+};
+WorkspaceLayout workspace_layout(int64_t batch_per_launch, int64_t num_heads_k, int64_t group,
+                                 int grid_max);
+
+// Launchers.  dtype: 0 bf16, 1 fp16; out_fp32 selects an fp32 output.
+cudaError_t launch_decode_sm100(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                                const CUtensorMap& tm_v, const DecodeParams& p, int dtype,
+                                bool out_fp32, int grid, cudaStream_t stream);
+cudaError_t launch_decode_simt(const SimtParams& p, int dtype, bool out_fp32, cudaStream_t stream);
+cudaError_t launch_combine_lse(const float* part_o, const float* part_lse, int64_t n_parts,
+                               int64_t rows, int64_t head_dim, void* out, int out_dtype,
+                               float* lse_out, cudaStream_t stream);
+
+cudaError_t launch_bounded_wait_probe(unsigned long long budget_ns, int* status,
+                                      unsigned long long* waited_ns, cudaStream_t stream);
+
+size_t sm100_smem_bytes();
+
+}  // namespace fd

@@ -1,0 +1,140 @@
+"""Torch-facing host API of the paged-KV GQA decode operator.
+
+``run_kernel`` mirrors the reference binding ``run_kernel_torch``
+(scripts/evaluate_flashattn_submission.py:46-78): same argument names and
+order, tensors in, pointers forwarded to the C ABI, nothing returned, and
+arguments the operator rejects are ignored silently exactly as the reference
+does (``last_error()`` tells why).
+
+``flash_decode`` is the extended call with the ``flash_attn_with_kvcache``
+argument vocabulary the reference's evaluator uses for its oracle
+(evaluate_flashattn_submission.py:232-247): q, k_cache, v_cache,
+cache_seqlens, block_table, softmax_scale, return_softmax_lse.  It runs on
+the tensors' device and current stream and raises on any error.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ._lib import (FD_DTYPE_BF16, FD_DTYPE_FP16, FD_DTYPE_FP32, FlashDecodeError, check,
+                   load_library)
+
+_DTYPES = {torch.bfloat16: FD_DTYPE_BF16, torch.float16: FD_DTYPE_FP16}
+_OUT_DTYPES = {torch.bfloat16: FD_DTYPE_BF16, torch.float16: FD_DTYPE_FP16, torch.float32: FD_DTYPE_FP32}
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if not t.is_cuda:
+            raise ValueError("flashdecode runs on CUDA tensors only (no CPU path)")
+
+
+def run_kernel(q, k_cache_paged, v_cache_paged, output, cache_seqlens, block_table, batch_size,
+               seqlen_k, seqlen_q, num_heads, num_heads_k, headdim, page_block_size, num_blocks,
+               causal) -> None:
+    """Reference operator surface: bf16, scale 1/sqrt(headdim), default stream."""
+    lib = load_library()
+    lib.run_kernel(_ptr(q), _ptr(k_cache_paged), _ptr(v_cache_paged), _ptr(output),
+                   _ptr(cache_seqlens), _ptr(block_table), int(batch_size), int(seqlen_k),
+                   int(seqlen_q), int(num_heads), int(num_heads_k), int(headdim),
+                   int(page_block_size), int(num_blocks), int(causal))
+
+
+def last_error() -> tuple[int, str]:
+    """(status, message) of the last C-ABI call on this thread."""
+    lib = load_library()
+    return int(lib.fd_last_error()), lib.fd_last_error_message().decode()
+
+
+def device_status() -> int:
+    """Read and clear the device error word of the library-owned workspace."""
+    return int(load_library().fd_device_status())
+
+
+def workspace_size(batch_size: int, num_heads: int, num_heads_k: int, headdim: int = 128) -> int:
+    return int(load_library().fd_decode_workspace_size(batch_size, num_heads, num_heads_k, headdim))
+
+
+def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                 cache_seqlens: torch.Tensor, block_table: torch.Tensor,
+                 softmax_scale: float | None = None, return_softmax_lse: bool = False,
+                 out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
+                 max_seqlen_k: int | None = None, workspace: torch.Tensor | None = None,
+                 stream: torch.cuda.Stream | None = None):
+    """Single-token paged decode attention.
+
+    q [B, 1, Hq, D]; k_cache/v_cache [num_blocks, page, Hkv, D];
+    cache_seqlens [B] int32; block_table [B, max_blocks] int32.
+    Returns out [B, 1, Hq, D] (and lse [B, Hq] fp32, natural log).
+    """
+    lib = load_library()
+    _require_cuda(q, k_cache, v_cache, cache_seqlens, block_table)
+    if q.dim() != 4 or q.shape[1] != 1:
+        raise ValueError(f"q must be [B, 1, Hq, D], got {tuple(q.shape)}")
+    if q.dtype not in _DTYPES or k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
+        raise ValueError("q, k_cache, v_cache must share dtype bf16 or fp16")
+    if cache_seqlens.dtype != torch.int32 or block_table.dtype != torch.int32:
+        raise ValueError("cache_seqlens and block_table must be int32")
+    for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache),
+                    ("cache_seqlens", cache_seqlens), ("block_table", block_table)):
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    B, _, Hq, D = q.shape
+    num_blocks, page, Hkv, Dk = k_cache.shape
+    if tuple(v_cache.shape) != tuple(k_cache.shape) or Dk != D:
+        raise ValueError("k_cache/v_cache shape mismatch")
+    if block_table.dim() != 2 or block_table.shape[0] != B or cache_seqlens.shape != (B,):
+        raise ValueError("block_table must be [B, max_blocks] and cache_seqlens [B]")
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    odt = q.dtype if out_dtype is None else out_dtype
+    if out is None:
+        out = torch.empty((B, 1, Hq, D), dtype=odt, device=q.device)
+    elif out.dtype != odt or tuple(out.shape) != (B, 1, Hq, D) or not out.is_contiguous():
+        raise ValueError("out has the wrong shape, dtype or layout")
+    lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device) if return_softmax_lse else None
+    ws_ptr, ws_bytes = None, 0
+    if workspace is not None:
+        ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    st = stream if stream is not None else torch.cuda.current_stream(q.device)
+    with torch.cuda.device(q.device):
+        status = lib.fd_decode_paged(
+            _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out), _ptr(lse), _ptr(cache_seqlens),
+            _ptr(block_table), int(block_table.shape[1]), B, Hq, Hkv, D, page, num_blocks,
+            _DTYPES[q.dtype], _OUT_DTYPES[odt], scale, int(max_seqlen_k or 0), ws_ptr, ws_bytes,
+            st.cuda_stream)
+    check(status)
+    return (out, lse) if return_softmax_lse else out
+
+
+def combine_lse(part_o: torch.Tensor, part_lse: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,
+                return_lse: bool = False, stream: torch.cuda.Stream | None = None):
+    """Merge partial results over disjoint KV ranges.
+
+    part_o [n, rows, D] fp32 (normalised), part_lse [n, rows] fp32 natural log.
+    Returns out [rows, D] (and lse [rows]).
+    """
+    lib = load_library()
+    _require_cuda(part_o, part_lse)
+    if part_o.dtype != torch.float32 or part_lse.dtype != torch.float32:
+        raise ValueError("partials must be fp32")
+    part_o = part_o.contiguous()
+    part_lse = part_lse.contiguous()
+    n, rows, D = part_o.shape
+    out = torch.empty((rows, D), dtype=out_dtype, device=part_o.device)
+    lse = torch.empty((rows,), dtype=torch.float32, device=part_o.device) if return_lse else None
+    st = stream if stream is not None else torch.cuda.current_stream(part_o.device)
+    with torch.cuda.device(part_o.device):
+        status = lib.fd_combine_lse(_ptr(part_o), _ptr(part_lse), n, rows, D, _ptr(out),
+                                    _OUT_DTYPES[out_dtype], _ptr(lse), st.cuda_stream)
+    check(status)
+    return (out, lse) if return_lse else out
+
+
+__all__ = ["run_kernel", "flash_decode", "combine_lse", "last_error", "device_status",
+           "workspace_size", "FlashDecodeError"]

@@ -1,0 +1,146 @@
+/*
+ * flashdecode.h - C ABI of the B200 (sm_100a) paged-KV GQA decode operator.
+ *
+ * All pointers are device pointers unless stated otherwise.  No torch types
+ * appear here; the library is loadable with dlopen/ctypes/cgo alike.
+ *
+ * Tensor layouts (row-major, contiguous):
+ *   q             [B, 1, Hq, D]                 (bf16 or fp16)
+ *   k_cache/v_cache [num_blocks, page, Hkv, D]  (same dtype as q, "NHD")
+ *   block_table   [B, block_table_stride]       int32 physical page ids
+ *   cache_seqlens [B]                           int32 tokens per sequence
+ *   out           [B, 1, Hq, D]                 (dtype of q, or fp32)
+ *   lse           [B, Hq]                       fp32 natural-log LSE (nullable)
+ * Query head h reads KV head h / (Hq / Hkv).  Entries of block_table past
+ * ceil(cache_seqlens[b] / page) are never read (they may be -1).
+ */
+#ifndef FLASHDECODE_H_
+#define FLASHDECODE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes */
+#define FD_DTYPE_BF16 0
+#define FD_DTYPE_FP16 1
+#define FD_DTYPE_FP32 2 /* output only */
+
+/* status codes */
+#define FD_OK 0
+#define FD_ERR_INVALID_ARG 1    /* a size/shape argument is out of range     */
+#define FD_ERR_UNSUPPORTED 2    /* valid request this build does not handle  */
+#define FD_ERR_WORKSPACE 3      /* workspace missing or too small            */
+#define FD_ERR_CUDA 4           /* a CUDA runtime/driver call failed         */
+#define FD_ERR_DEVICE_TIMEOUT 5 /* a bounded in-kernel wait ran out          */
+
+/*
+ * run_kernel - drop-in for the reference operator surface.
+ *
+ * Replaces: the `extern "C" void run_kernel(...)` declared by the reference
+ * evaluator's binding (scripts/evaluate_flashattn_submission.py:29-44) and
+ * defined by every submission, e.g.
+ * submission-oj/best_flashattn_kvcache_decode.cu:1186-1426.
+ * Same 15 arguments and meaning: bf16 tensors, softmax scale 1/sqrt(headdim),
+ * block_table row stride = num_blocks / batch_size, seqlen_k is the maximum
+ * sequence length (a scheduling hint; per-row lengths come from
+ * cache_seqlens), no LSE output, launched on the legacy default stream,
+ * asynchronous.  Like the reference it returns void and silently does nothing
+ * on arguments it rejects; unlike the reference the reason is kept and can be
+ * read with fd_last_error().  Unsupported-by-the-reference shapes (any head
+ * group, page sizes other than 16, fp16 is not reachable here) are computed
+ * rather than rejected.  seqlen_q must be 1 and causal is accepted and has no
+ * effect for a single query token (the reference falls back to a kernel that
+ * also assumes one query token).
+ */
+void run_kernel(const void* q, const void* k_cache_paged, const void* v_cache_paged, void* output,
+                const int32_t* cache_seqlens, const int32_t* block_table, int64_t batch_size,
+                int64_t seqlen_k, int64_t seqlen_q, int64_t num_heads, int64_t num_heads_k,
+                int64_t headdim, int64_t page_block_size, int64_t num_blocks, int64_t causal);
+
+/*
+ * fd_decode_paged - the extended entry point (stream, dtype, scale, LSE,
+ * explicit block_table stride, caller workspace).
+ *
+ * Replaces: the same reference run_kernel (best_flashattn_kvcache_decode.cu
+ * :1186-1426) with the arguments the reference hard-codes made explicit:
+ * softmax scale (best :286-287), block_table stride (best :1213), stream
+ * (reference launches on the default stream), LSE output (reference emits
+ * none; flash_attn_with_kvcache's return_softmax_lse, which the evaluator's
+ * oracle call at evaluate_flashattn_submission.py:232-247 wraps).
+ *
+ * dtype:        FD_DTYPE_BF16 or FD_DTYPE_FP16 for q/k/v.
+ * out_dtype:    FD_DTYPE_FP32 or the value of dtype.
+ * max_seqlen_k: upper bound on cache_seqlens (0 = unknown); only sizes the grid.
+ * workspace:    device buffer of at least fd_decode_workspace_size(...) bytes,
+ *               zero-filled before its first use (the operator leaves it
+ *               zeroed after every successful call), or NULL to use a
+ *               library-owned per-device buffer.  One workspace must not be
+ *               used by two calls that can run at the same time.
+ * stream:       cudaStream_t (NULL = legacy default stream).
+ * Returns FD_OK or an FD_ERR_* code; launches are asynchronous.
+ */
+int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, void* out, float* lse,
+                    const int32_t* cache_seqlens, const int32_t* block_table,
+                    int64_t block_table_stride, int64_t batch_size, int64_t num_heads,
+                    int64_t num_heads_k, int64_t headdim, int64_t page_block_size,
+                    int64_t num_blocks, int dtype, int out_dtype, float softmax_scale,
+                    int64_t max_seqlen_k, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * fd_decode_workspace_size - bytes of workspace fd_decode_paged needs for
+ * these shapes on the current device.
+ * Replaces: reserve_split_workspace sizing (best :1078-1133, :1343-1348),
+ * exposed so callers can own the memory.
+ */
+size_t fd_decode_workspace_size(int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
+                                int64_t headdim);
+
+/*
+ * fd_combine_lse - merge n_parts partial attention results computed over
+ * disjoint KV ranges into one (the cross-GPU split-KV exchange step).
+ * part_o   [n_parts, rows, headdim] fp32, each part already normalised;
+ * part_lse [n_parts, rows] fp32 natural log (-inf = empty part);
+ * out      [rows, headdim] of out_dtype; lse_out [rows] (nullable).
+ * Replaces: combine_split_lse_kernel (best :956-1037) and combine_lse_kernel
+ * _v11 (v11_best_hybrid/..._v11_best_hybrid.cu:574-614), including the rule
+ * that empty parts get weight zero.
+ */
+int fd_combine_lse(const float* part_o, const float* part_lse, int64_t n_parts, int64_t rows,
+                   int64_t headdim, void* out, int out_dtype, float* lse_out, void* stream);
+
+/* Status of the last call made on this host thread, and its message. */
+int fd_last_error(void);
+const char* fd_error_string(int code);
+const char* fd_last_error_message(void);
+
+/*
+ * fd_device_status - read and clear the device-side error word of the
+ * library-owned workspace of the current device (FD_ERR_DEVICE_TIMEOUT if a
+ * bounded wait inside a kernel ran out since the last read).  Synchronises
+ * the current device.
+ */
+int fd_device_status(void);
+
+/*
+ * fd_selftest_bounded_wait - launch a one-warp kernel that waits on an
+ * mbarrier nothing arrives on, with the same bounded wait the decode kernel
+ * uses, and report what happened.  Returns FD_ERR_DEVICE_TIMEOUT when the
+ * wait gave up as designed (the CUDA context stays usable), FD_OK if the
+ * barrier completed, FD_ERR_CUDA on a launch failure.  *waited_ns (nullable,
+ * host pointer) receives the time the wait took.  Synchronises the device.
+ * No counterpart in the reference, which has no bounded waits.
+ */
+int fd_selftest_bounded_wait(uint64_t budget_ns, uint64_t* waited_ns);
+
+/* Library version string. */
+const char* fd_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASHDECODE_H_ */

@@ -1,0 +1,120 @@
+"""CPU oracle for paged-KV GQA decode attention.
+
+TEST INFRASTRUCTURE ONLY.  Only tests/, __graft_entry__.smoke() and the
+cpu_baseline / --impl reference legs of bench.py may import this module, and
+only as the checker or as the timed CPU baseline.  The operator itself never
+calls it: there is no CPU fallback.
+
+What it restates: the reference's decode semantics for one query token,
+    s_t   = scale * q . k_t              for t < cache_seqlens[b]
+    O     = sum_t softmax(s)_t v_t,      LSE = ln sum_t exp(s_t)
+with k_t / v_t found through the page table (page = block_table[b, t // bs],
+row t % bs, KV head h // (Hq / Hkv)), following
+  - the math of the reference kernels: QK dot and scale
+    (submission-oj/best_flashattn_kvcache_decode.cu:286-287, :398-400),
+    softmax/merge (:541-578, :838-953), split combine (:956-1037);
+  - the page-table gather (best :266-271, :741-742) and GQA head mapping
+    (best :250, :653);
+  - edge rules: length <= 0 gives O = 0 (best :256-260, :422-430) and
+    LSE = -inf, length 1 returns the single V row (best :273-284, :443-460);
+  - the numpy restatement in submission-oj/diagnostics/diag_integrated.py:48-57.
+The reference's own oracle is flash_attn_with_kvcache
+(scripts/evaluate_flashattn_submission.py:232-247; flash_attn 2.6.3 on its
+box, 2.8.3 here), a CUDA-only library; tests/golden/ holds its outputs on
+seeded inputs, against which this oracle is pinned.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+
+def decode_reference(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     cache_seqlens: torch.Tensor, block_table: torch.Tensor,
+                     softmax_scale: float | None = None, rows=None,
+                     compute_dtype: torch.dtype = torch.float32):
+    """Vectorised oracle (torch on CPU).
+
+    q [B, 1, Hq, D]; k_cache/v_cache [num_blocks, page, Hkv, D];
+    cache_seqlens [B]; block_table [B, max_blocks].
+    Returns (out [B, 1, Hq, D], lse [B, Hq]) in compute_dtype; rows not in
+    `rows` (when given) are left zero / -inf.
+    """
+    q = q.cpu()
+    B, _, Hq, D = q.shape
+    _, page, Hkv, _ = k_cache.shape
+    G = Hq // Hkv
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    seqlens = cache_seqlens.cpu().tolist()
+    bt = block_table.cpu()
+    out = torch.zeros((B, 1, Hq, D), dtype=compute_dtype)
+    lse = torch.full((B, Hq), float("-inf"), dtype=compute_dtype)
+    for b in (range(B) if rows is None else rows):
+        L = max(0, int(seqlens[b]))
+        if L == 0:
+            continue
+        n_pages = (L + page - 1) // page
+        pages = bt[b, :n_pages].long()
+        K = k_cache[pages.to(k_cache.device)].cpu().reshape(n_pages * page, Hkv, D)[:L].to(compute_dtype)
+        V = v_cache[pages.to(v_cache.device)].cpu().reshape(n_pages * page, Hkv, D)[:L].to(compute_dtype)
+        qb = q[b, 0].to(compute_dtype).reshape(Hkv, G, D)
+        s = torch.einsum("hgd,lhd->hgl", qb, K) * scale
+        m = s.amax(dim=-1, keepdim=True)
+        e = torch.exp(s - m)
+        den = e.sum(dim=-1, keepdim=True)
+        o = torch.einsum("hgl,lhd->hgd", e / den, V)
+        out[b, 0] = o.reshape(Hq, D)
+        lse[b] = (m + torch.log(den)).reshape(Hq)
+    return out, lse
+
+
+def decode_reference_loops(q, k_cache, v_cache, cache_seqlens, block_table,
+                           softmax_scale: float | None = None):
+    """Independent scalar restatement in float64 pure-Python loops (small cases only)."""
+    qf = q.double().tolist()
+    kf = k_cache.double().tolist()
+    vf = v_cache.double().tolist()
+    B, Hq, D = len(qf), len(qf[0][0]), len(qf[0][0][0])
+    page, Hkv = len(kf[0]), len(kf[0][0])
+    G = Hq // Hkv
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    out = [[[0.0] * D for _ in range(Hq)] for _ in range(B)]
+    lse = [[float("-inf")] * Hq for _ in range(B)]
+    for b in range(B):
+        L = max(0, int(cache_seqlens[b]))
+        for h in range(Hq):
+            kvh = h // G
+            scores, vals = [], []
+            for t in range(L):
+                pg = int(block_table[b][t // page])
+                krow = kf[pg][t % page][kvh]
+                scores.append(scale * sum(qf[b][0][h][d] * krow[d] for d in range(D)))
+                vals.append(vf[pg][t % page][kvh])
+            if L == 0:
+                continue
+            m = max(scores)
+            w = [math.exp(s - m) for s in scores]
+            tot = sum(w)
+            lse[b][h] = m + math.log(tot)
+            out[b][h] = [sum(w[t] * vals[t][d] for t in range(L)) / tot for d in range(D)]
+    return (torch.tensor(out, dtype=torch.float64).reshape(B, 1, Hq, D),
+            torch.tensor(lse, dtype=torch.float64))
+
+
+def merge_partials(part_o: torch.Tensor, part_lse: torch.Tensor):
+    """Merge normalised partials over disjoint KV ranges (natural-log LSE).
+
+    Restates the reference's combine (best :956-1037): weights
+    exp(lse_j - max lse), parts with lse = -inf weigh zero.
+    """
+    po = part_o.double()
+    pl = part_lse.double()
+    mx = pl.amax(dim=0)
+    mx_safe = torch.where(torch.isinf(mx), torch.zeros_like(mx), mx)
+    w = torch.where(torch.isinf(pl), torch.zeros_like(pl), torch.exp(pl - mx_safe))
+    den = w.sum(dim=0)
+    out = (w.unsqueeze(-1) * torch.nan_to_num(po)).sum(dim=0) / den.clamp(min=1e-300).unsqueeze(-1)
+    out = torch.where(den.unsqueeze(-1) > 0, out, torch.zeros_like(out))
+    lse = torch.where(den > 0, mx_safe + torch.log(den.clamp(min=1e-300)), torch.full_like(den, float("-inf")))
+    return out, lse

@@ -1,0 +1,224 @@
+"""GPU parity of the CUDA operator against the CPU oracle (and, where it runs,
+against the reference's own oracle flash_attn_with_kvcache).
+
+Tolerances: output within atol 2e-3 / rtol 1e-2 of the
+fp32 oracle, LSE (natural log) within 1e-3; page-table gathers exact
+(one-hot and single-token cases compare bit-for-bit)."""
+import math
+
+import pytest
+import torch
+
+import flashdecode
+from flashdecode import cases
+from oracle.decode_ref import decode_reference, merge_partials
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL, LSE_ATOL = 2e-3, 1e-2, 1e-3
+
+
+def run(t, c, **kw):
+    return flashdecode.flash_decode(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"],
+                                    t["block_table"], softmax_scale=c.softmax_scale, **kw)
+
+
+def check(c, t, out, lse=None, rows=None):
+    ref_o, ref_l = decode_reference(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"],
+                                    t["block_table"], softmax_scale=c.softmax_scale, rows=rows)
+    sel = list(range(c.B)) if rows is None else list(rows)
+    got = out.float().cpu()[sel]
+    exp = ref_o[sel]
+    err = (got - exp).abs()
+    bad = err > ATOL + RTOL * exp.abs()
+    assert not bad.any(), f"{c.name}: {int(bad.sum())} elements off, max err {float(err.max()):.3e}"
+    if lse is not None:
+        gl, el = lse.cpu()[sel], ref_l[sel]
+        fin = torch.isfinite(el)
+        assert torch.equal(fin, torch.isfinite(gl)), f"{c.name}: LSE finiteness differs"
+        assert torch.allclose(gl[fin], el[fin], atol=LSE_ATOL), f"{c.name}: LSE off"
+
+
+RAGGED = [1, 127, 128, 129, 300, 0, 1000, 2049]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("Hq,Hkv", [(32, 8), (64, 8), (28, 4), (8, 8), (16, 1)])
+@pytest.mark.parametrize("page", [256, 16, 64])
+def test_small_parity(dtype, Hq, Hkv, page):
+    c = cases.custom_case(f"small_{Hq}_{Hkv}_{page}", dtype, RAGGED, Hq, Hkv, page=page, seed=Hq + page)
+    t = cases.materialize(c, "cuda", seed=7)
+    out, lse = run(t, c, return_softmax_lse=True)
+    torch.cuda.synchronize()
+    check(c, t, out, lse)
+
+
+@pytest.mark.parametrize("page", [32, 48, 128, 512])
+def test_other_page_sizes(page):
+    c = cases.custom_case(f"page{page}", torch.bfloat16, [5, 700, 1537, 64], 32, 8, page=page, seed=page)
+    t = cases.materialize(c, "cuda", seed=3)
+    out, lse = run(t, c, return_softmax_lse=True)
+    check(c, t, out, lse)
+
+
+def test_fp32_output_and_scale():
+    c = cases.custom_case("fp32out", torch.bfloat16, [900, 33, 4096], 32, 8, seed=11)
+    c.softmax_scale = 0.05
+    t = cases.materialize(c, "cuda", seed=11)
+    out, lse = run(t, c, return_softmax_lse=True, out_dtype=torch.float32)
+    assert out.dtype == torch.float32
+    check(c, t, out, lse)
+
+
+@pytest.mark.parametrize("D,Hq,Hkv,page", [(64, 16, 4, 16), (256, 8, 8, 16), (128, 32, 1, 16),
+                                           (128, 8, 2, 8), (32, 4, 2, 1)])
+def test_simt_path_shapes(D, Hq, Hkv, page):
+    """Head dims != 128, groups > 16 and pages not a multiple of 16 take the CUDA-core kernel."""
+    c = cases.custom_case(f"simt_{D}_{Hq}_{Hkv}_{page}", torch.float16, [1, 0, 77, 513], Hq, Hkv,
+                          D=D, page=page, seed=D)
+    t = cases.materialize(c, "cuda", seed=5)
+    out, lse = run(t, c, return_softmax_lse=True)
+    check(c, t, out, lse)
+
+
+def test_single_token_sequences_return_v_exactly():
+    c = cases.custom_case("len1", torch.bfloat16, [1] * 9, 32, 8, seed=2)
+    t = cases.materialize(c, "cuda", seed=2)
+    out = run(t, c)
+    for b in range(c.B):
+        pg = int(c.block_table[b, 0])
+        for h in range(32):
+            assert torch.equal(out[b, 0, h], t["v_cache"][pg, 0, h // 4]), (b, h)
+
+
+@pytest.mark.parametrize("page", [256, 16])
+def test_one_hot_gather_bit_exact(page):
+    """K = 0 except one token per (b, kv head) aligned with q: O is that V row."""
+    c = cases.custom_case("onehot", torch.bfloat16, [3000, 129, 17, 1024], 32, 8, page=page, seed=9)
+    t = cases.materialize(c, "cuda", seed=9)
+    t["k_cache"].zero_()
+    hot = {0: 2999, 1: 64, 2: 0, 3: 777}
+    for b, tok in hot.items():
+        pg = int(c.block_table[b, tok // page])
+        for kvh in range(8):
+            qh = t["q"][b, 0, kvh * 4]
+            t["q"][b, 0, kvh * 4: kvh * 4 + 4] = qh
+            t["k_cache"][pg, tok % page, kvh] = qh * 16
+    out = run(t, c)
+    for b, tok in hot.items():
+        pg = int(c.block_table[b, tok // page])
+        for h in range(32):
+            assert torch.equal(out[b, 0, h], t["v_cache"][pg, tok % page, h // 4]), (b, h)
+
+
+def test_nan_in_unused_cache_rows_does_not_leak():
+    """Cache rows past a sequence's end (same page) hold NaN: output stays finite and exact."""
+    c = cases.custom_case("nan_tail", torch.bfloat16, [130, 5, 300], 32, 8, page=256, seed=4)
+    t = cases.materialize(c, "cuda", seed=4)
+    out_ref = run(t, c).clone()
+    for b in range(c.B):
+        L = int(c.seqlens[b])
+        pg = int(c.block_table[b, (L - 1) // 256])
+        t["k_cache"][pg, L % 256:] = float("nan")
+        t["v_cache"][pg, L % 256:] = float("nan")
+    out = run(t, c)
+    assert torch.isfinite(out.float()).all()
+    assert torch.equal(out, out_ref)
+
+
+def test_deterministic():
+    c = cases.config_case(3)
+    t = cases.materialize(c, "cuda")
+    a = run(t, c).clone()
+    b = run(t, c)
+    assert torch.equal(a, b)
+
+
+def test_caller_workspace_and_size_check():
+    c = cases.custom_case("ws", torch.bfloat16, [5000, 17, 9000], 32, 8, seed=6)
+    t = cases.materialize(c, "cuda", seed=6)
+    n = flashdecode.workspace_size(c.B, c.Hq, c.Hkv)
+    assert n > 0
+    ws = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    out1, lse1 = run(t, c, return_softmax_lse=True, workspace=ws)
+    out2, lse2 = run(t, c, return_softmax_lse=True)
+    assert torch.equal(out1, out2) and torch.equal(lse1, lse2)
+    check(c, t, out1, lse1)
+    with pytest.raises(flashdecode.FlashDecodeError) as ei:
+        run(t, c, workspace=ws[: n // 2])
+    assert ei.value.code == 3
+
+
+def test_wrong_max_seqlen_hint_still_correct():
+    c = cases.custom_case("hint", torch.bfloat16, [3000, 5, 12000], 32, 8, seed=8)
+    t = cases.materialize(c, "cuda", seed=8)
+    out, lse = run(t, c, return_softmax_lse=True, max_seqlen_k=1)
+    check(c, t, out, lse)
+
+
+def test_batch_larger_than_one_launch():
+    g = torch.Generator().manual_seed(1)
+    sl = torch.randint(0, 400, (2500,), generator=g).tolist()
+    c = cases.custom_case("bigbatch", torch.float16, sl, 8, 2, page=16, seed=1)
+    t = cases.materialize(c, "cuda", seed=1)
+    out, lse = run(t, c, return_softmax_lse=True)
+    check(c, t, out, lse, rows=[0, 1, 2047, 2048, 2049, 2499])
+
+
+@pytest.mark.parametrize("shape", cases.CONTEST_SHAPES)
+def test_reference_abi_contest_shapes(shape):
+    """The 15-argument run_kernel on the reference's contest profile."""
+    B, L, Hkv = shape
+    c = cases.contest_case(B, L, Hkv)
+    t = cases.materialize(c, "cuda", seed=0)
+    out = torch.zeros_like(t["q"])
+    flashdecode.run_kernel(t["q"], t["k_cache"], t["v_cache"], out, t["cache_seqlens"],
+                           t["block_table"], B, L, 1, 32, Hkv, 128, 16, c.num_blocks, 0)
+    torch.cuda.synchronize()
+    assert flashdecode.last_error()[0] == 0
+    check(c, t, out)
+
+
+@pytest.mark.parametrize("idx", [1, 2, 3, 4, 5])
+def test_baseline_configs(idx):
+    """Full-size BASELINE configs: sampled rows against the oracle, all rows finite."""
+    c = cases.config_case(idx)
+    t = cases.materialize(c, "cuda")
+    out, lse = run(t, c, return_softmax_lse=True)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all() and torch.isfinite(lse).all()
+    order = sorted(range(c.B), key=lambda b: int(c.seqlens[b]))
+    rows = sorted({order[0], order[-1], order[len(order) // 2], 0, c.B - 1})
+    check(c, t, out, lse, rows=rows)
+
+
+def test_combine_lse_matches_oracle_merge():
+    g = torch.Generator().manual_seed(0)
+    n, rows, D = 5, 37, 128
+    po = torch.randn(n, rows, D, generator=g)
+    pl = torch.randn(n, rows, generator=g) * 3
+    pl[1, :5] = float("-inf")
+    pl[:, 7] = float("-inf")
+    out, lse = flashdecode.combine_lse(po.cuda(), pl.cuda(), out_dtype=torch.float32, return_lse=True)
+    eo, el = merge_partials(po, pl)
+    assert torch.allclose(out.cpu(), eo.float(), atol=1e-5, rtol=1e-5)
+    fin = torch.isfinite(el)
+    assert torch.equal(fin, torch.isfinite(lse.cpu()))
+    assert torch.allclose(lse.cpu()[fin], el.float()[fin], atol=1e-5)
+
+
+def test_against_flash_attn_reference_oracle():
+    """The reference evaluator's oracle (flash_attn_with_kvcache) on config 2."""
+    fa = pytest.importorskip("flash_attn.flash_attn_interface")
+    c = cases.config_case(2)
+    t = cases.materialize(c, "cuda")
+    try:
+        ref, ref_lse = fa.flash_attn_with_kvcache(
+            t["q"], t["k_cache"], t["v_cache"], None, None, cache_seqlens=t["cache_seqlens"],
+            block_table=t["block_table"], causal=False, num_splits=0, return_softmax_lse=True)
+    except RuntimeError as e:  # e.g. no kernel image for this GPU
+        pytest.skip(f"flash_attn unavailable on this device: {e}")
+    out, lse = run(t, c, return_softmax_lse=True)
+    err = (out.float() - ref.float()).abs()
+    assert (err <= ATOL + RTOL * ref.float().abs()).all(), float(err.max())
+    assert torch.allclose(lse, ref_lse.reshape(c.B, c.Hq).float(), atol=LSE_ATOL)
