@@ -16,6 +16,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "../../include/flashdecode.h"
@@ -25,6 +26,7 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 constexpr unsigned long long kDefaultTimeoutNs = 1000000000ull;  // 1 s per in-kernel wait
+constexpr int kDefaultPrefetchTiles = 4;
 
 thread_local int t_last_error = FD_OK;
 thread_local char t_last_msg[256] = "ok";
@@ -127,6 +129,28 @@ CUresult encode(CUtensorMap* m, int dtype, int rank, const void* base, const cuu
                      static_cast<cuuint32_t>(rank), const_cast<void*>(base), dims, strides, box,
                      estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+// Launch epoch for the split-pair arrival counters: consecutive launches get
+// different values in 1 .. 2^20-1 (0 never occurs, so a zeroed workspace
+// reads as "no arrivals").
+uint32_t next_epoch() {
+  static std::atomic<uint32_t> counter{0};
+  return counter.fetch_add(1, std::memory_order_relaxed) % 0xFFFFFu + 1u;
+}
+
+// L2 prefetch distance of the tensor-core kernel, in 128-token tiles
+// (FD_PREFETCH_TILES overrides; 0 disables).
+int prefetch_tiles() {
+  static int v = [] {
+    const char* e = std::getenv("FD_PREFETCH_TILES");
+    if (e != nullptr) {
+      const long x = std::strtol(e, nullptr, 10);
+      if (x >= 0 && x <= 64) return static_cast<int>(x);
+    }
+    return kDefaultPrefetchTiles;
+  }();
+  return v;
 }
 
 unsigned long long timeout_ns() {
@@ -301,6 +325,8 @@ int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, voi
     p.part_lse = reinterpret_cast<float*>(ws + wl.lse_off);
     p.part_o = reinterpret_cast<float*>(ws + wl.o_off);
     p.timeout_ns = timeout_ns();
+    p.epoch = next_epoch();
+    p.prefetch_tiles = prefetch_tiles();
     const int64_t work_bound = nb * num_heads_k * tiles_bound;
     const int grid = static_cast<int>(work_bound < sms ? work_bound : sms);
     const cudaError_t e = fd::launch_decode_sm100(tm_q, tm_k, tm_v, p, dtype, out_fp32, grid, st);
@@ -334,16 +360,22 @@ void run_kernel(const void* q, const void* k_cache_paged, const void* v_cache_pa
                   num_blocks, FD_DTYPE_BF16, FD_DTYPE_BF16, scale, seqlen_k, nullptr, 0, nullptr);
 }
 
-int fd_combine_lse(const float* part_o, const float* part_lse, int64_t n_parts, int64_t rows,
-                   int64_t headdim, void* out, int out_dtype, float* lse_out, void* stream) {
+int fd_combine_lse(const float* part_o, int64_t part_o_stride, const float* part_lse,
+                   int64_t part_lse_stride, int64_t n_parts, int64_t rows, int64_t headdim,
+                   void* out, int out_dtype, float* lse_out, void* stream) {
   if (part_o == nullptr || part_lse == nullptr || out == nullptr)
     return set_error(FD_ERR_INVALID_ARG, "null pointer");
   if (n_parts <= 0 || rows < 0 || headdim <= 0 || rows > INT32_MAX)
     return set_error(FD_ERR_INVALID_ARG, "bad sizes");
+  if (part_o_stride == 0) part_o_stride = rows * headdim;
+  if (part_lse_stride == 0) part_lse_stride = rows;
+  if (part_o_stride < rows * headdim || part_lse_stride < rows)
+    return set_error(FD_ERR_INVALID_ARG, "part strides overlap the parts");
   if (out_dtype != FD_DTYPE_BF16 && out_dtype != FD_DTYPE_FP16 && out_dtype != FD_DTYPE_FP32)
     return set_error(FD_ERR_INVALID_ARG, "bad out_dtype");
-  const cudaError_t e = fd::launch_combine_lse(part_o, part_lse, n_parts, rows, headdim, out,
-                                               out_dtype, lse_out, static_cast<cudaStream_t>(stream));
+  const cudaError_t e =
+      fd::launch_combine_lse(part_o, part_o_stride, part_lse, part_lse_stride, n_parts, rows,
+                             headdim, out, out_dtype, lse_out, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "combine launch: %s", cudaGetErrorString(e));
   return set_ok();
 }

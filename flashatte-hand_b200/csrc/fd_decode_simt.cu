@@ -123,28 +123,29 @@ __global__ void __launch_bounds__(32 * kSimtWarps)
 }
 
 // out[r] = sum_j w_j o_j[r] / sum_j w_j with w_j = exp(lse_j - max lse),
-// parts with lse = -inf weigh zero (their O is never read).
+// parts with lse = -inf weigh zero (their O is never read).  Part j of O
+// starts at part_o + j * o_stride, part j of LSE at part_lse + j * l_stride.
 template <typename OutT>
 __global__ void __launch_bounds__(128)
-    combine_lse_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
-                       int64_t n_parts, int64_t rows, int64_t head_dim, OutT* __restrict__ out,
-                       float* __restrict__ lse_out) {
+    combine_lse_kernel(const float* __restrict__ part_o, int64_t o_stride,
+                       const float* __restrict__ part_lse, int64_t l_stride, int64_t n_parts,
+                       int64_t head_dim, OutT* __restrict__ out, float* __restrict__ lse_out) {
   const int64_t r = blockIdx.x;
   const float neg_inf = -__int_as_float(0x7f800000);
   const float log2e = 1.4426950408889634f;
   float mx = neg_inf;
-  for (int64_t j = 0; j < n_parts; ++j) mx = fmaxf(mx, part_lse[j * rows + r]);
+  for (int64_t j = 0; j < n_parts; ++j) mx = fmaxf(mx, part_lse[j * l_stride + r]);
   float den = 0.f;
   for (int64_t j = 0; j < n_parts; ++j) {
-    const float lj = part_lse[j * rows + r];
+    const float lj = part_lse[j * l_stride + r];
     den += lj == neg_inf ? 0.f : fast_exp2((lj - mx) * log2e);
   }
   for (int64_t d = threadIdx.x; d < head_dim; d += blockDim.x) {
     float acc = 0.f;
     for (int64_t j = 0; j < n_parts; ++j) {
-      const float lj = part_lse[j * rows + r];
+      const float lj = part_lse[j * l_stride + r];
       if (lj == neg_inf) continue;
-      acc = fmaf(fast_exp2((lj - mx) * log2e), part_o[(j * rows + r) * head_dim + d], acc);
+      acc = fmaf(fast_exp2((lj - mx) * log2e), part_o[j * o_stride + r * head_dim + d], acc);
     }
     out[r * head_dim + d] = from_f32<OutT>(den > 0.f ? acc / den : 0.f);
   }
@@ -175,22 +176,25 @@ cudaError_t launch_decode_simt(const SimtParams& p, int dtype, bool out_fp32, cu
                   : launch_simt_typed<__half, __half>(p, stream);
 }
 
-cudaError_t launch_combine_lse(const float* part_o, const float* part_lse, int64_t n_parts,
-                               int64_t rows, int64_t head_dim, void* out, int out_dtype,
-                               float* lse_out, cudaStream_t stream) {
+cudaError_t launch_combine_lse(const float* part_o, int64_t o_stride, const float* part_lse,
+                               int64_t l_stride, int64_t n_parts, int64_t rows, int64_t head_dim,
+                               void* out, int out_dtype, float* lse_out, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   const dim3 grid(static_cast<unsigned>(rows));
   switch (out_dtype) {
     case 0:
       combine_lse_kernel<__nv_bfloat16><<<grid, 128, 0, stream>>>(
-          part_o, part_lse, n_parts, rows, head_dim, static_cast<__nv_bfloat16*>(out), lse_out);
+          part_o, o_stride, part_lse, l_stride, n_parts, head_dim, static_cast<__nv_bfloat16*>(out),
+          lse_out);
       break;
     case 1:
-      combine_lse_kernel<__half><<<grid, 128, 0, stream>>>(part_o, part_lse, n_parts, rows, head_dim,
+      combine_lse_kernel<__half><<<grid, 128, 0, stream>>>(part_o, o_stride, part_lse, l_stride,
+                                                           n_parts, head_dim,
                                                            static_cast<__half*>(out), lse_out);
       break;
     default:
-      combine_lse_kernel<float><<<grid, 128, 0, stream>>>(part_o, part_lse, n_parts, rows, head_dim,
+      combine_lse_kernel<float><<<grid, 128, 0, stream>>>(part_o, o_stride, part_lse, l_stride,
+                                                          n_parts, head_dim,
                                                           static_cast<float*>(out), lse_out);
       break;
   }

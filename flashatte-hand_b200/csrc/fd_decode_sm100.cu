@@ -40,8 +40,11 @@ constexpr int kHalfBytes = kTileTokens * 128;    // 128 tokens x 64 dims x 2 B =
 constexpr int kOperandBytes = 2 * kHalfBytes;    // one K or V tile: 32 KB
 constexpr int kStageBytes = 2 * kOperandBytes;   // K + V: 64 KB
 constexpr int kQSlotBytes = 2 * kMaxGroup * 128; // two halves x 16 rows x 128 B
-constexpr int kPBufBytes = kTileTokens * kMaxGroup * 2;  // 128 tokens x 16 heads x 2 B
-constexpr int kTmemCols = 64;                    // S0 S1 O0 O1, 16 columns each
+// P is stored as two 16-bit parts, P = hi + lo (hi = round(P), lo = round(P - hi)),
+// side by side in the UMMA N dimension: 128 tokens x (2 x 16 heads) x 2 B.
+// Summing V.hi and V.lo keeps P's fp32 precision through a 16-bit MMA.
+constexpr int kPBufBytes = kTileTokens * 2 * kMaxGroup * 2;
+constexpr int kTmemCols = 128;                   // S0 S1 (16 cols each), O0 O1 (32 each)
 constexpr int kNumBars = 2 * kStages + 14;
 
 // Shared-memory carve-up, offsets from a 1024-byte aligned base.
@@ -57,9 +60,24 @@ constexpr int kSmemUsed = kOffPrefix + (kMaxBatchPerLaunch + 1) * 4;
 constexpr int kSmemBytes = kSmemUsed + 1024;                 // slack for 1024-B alignment
 static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
 
-// TMEM columns: S^T of tile parity b at 16*b, O^T of tile parity b at 32+16*b.
+// TMEM columns: S^T of tile parity b at 16*b, O^T of tile parity b at 32+32*b.
 __device__ __forceinline__ uint32_t col_s(int b) { return static_cast<uint32_t>(b) * 16u; }
-__device__ __forceinline__ uint32_t col_o(int b) { return 32u + static_cast<uint32_t>(b) * 16u; }
+__device__ __forceinline__ uint32_t col_o(int b) { return 32u + static_cast<uint32_t>(b) * 32u; }
+
+// Arrival counter of a split (sequence, KV head) pair: bits [12, 32) hold the
+// launch epoch, bits [0, 12) the arrivals seen in that epoch.  A counter left
+// by any earlier launch (even one that stopped early) reads as zero, so the
+// workspace never needs clearing.  Returns true for the pair's last arrival.
+__device__ __forceinline__ bool ticket_arrive(uint32_t* t, uint32_t epoch, int nseg) {
+  uint32_t old = atomicAdd(t, 0u);
+  for (;;) {
+    const uint32_t cnt = (old >> 12) == epoch ? (old & 0xFFFu) : 0u;
+    const uint32_t nv = (epoch << 12) | (cnt + 1u);
+    const uint32_t prev = atomicCAS(t, old, nv);
+    if (prev == old) return cnt + 1u == static_cast<uint32_t>(nseg);
+    old = prev;
+  }
+}
 
 // UMMA shared-memory descriptor (tcgen05 matrix descriptor): start address,
 // leading/stride byte offsets (16-byte units), version 1, layout type.
@@ -84,19 +102,28 @@ __host__ __device__ constexpr uint32_t make_idesc(bool bf16, bool a_mn_major, bo
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// split2(a, b): hi = round-to-nearest 16-bit pair of (a, b), lo = the same
+// rounding of the residuals (a - hi.x, b - hi.y); hi + lo carries ~16 more
+// mantissa bits than hi alone.
 template <typename T> struct DType;
 template <> struct DType<__nv_bfloat16> {
   static constexpr bool kBf16 = true;
-  static __device__ __forceinline__ uint32_t pack2(float a, float b) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
+  static __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
   }
 };
 template <> struct DType<__half> {
   static constexpr bool kBf16 = false;
-  static __device__ __forceinline__ uint32_t pack2(float a, float b) {
-    __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
+  static __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
   }
 };
 
@@ -162,6 +189,9 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     decode_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const DecodeParams p) {
+  // P.V uses N = 2*NCOL columns: NCOL hi parts then NCOL lo parts of P.
+  constexpr int kPvN = 2 * NCOL;
+  constexpr int kPGroupBytes = (kPvN / 8) * 128;  // one 8-token group of P rows
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -251,11 +281,14 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   __syncthreads();
 
   const uint32_t tmem = *tmem_slot;
-  const int grid = gridDim.x;
   const int cta = blockIdx.x;
   const int64_t total = static_cast<int64_t>(hkv) * prefix[batch];
-  const int64_t w_begin = total * cta / grid;
-  const int64_t w_end = total * (cta + 1) / grid;
+  // The range split uses at most `total` CTAs, so every range is non-empty and
+  // the CTAs cta_of() counts for a pair all hold a segment of it.  CTAs past
+  // that (the host sized the grid from an upper bound) have nothing to do.
+  const int grid = total < static_cast<int64_t>(gridDim.x) ? static_cast<int>(total) : gridDim.x;
+  const int64_t w_begin = cta < grid ? total * cta / grid : 0;
+  const int64_t w_end = cta < grid ? total * (cta + 1) / grid : 0;
 
   if (warp == 0) {
     // ---------------------------------------------------------- TMA producer
@@ -268,6 +301,25 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     const uint64_t pol_keep = policy_evict_last();
     const int chunk = p.chunk;  // tokens per TMA box; never crosses a page
     const int nchunks = kTileTokens / chunk;
+    // L2 prefetch of the tile `pf_dist` tiles past the one being loaded into
+    // shared memory: the DRAM requests for upcoming tiles are in flight while
+    // the shared-memory ring is still full, and the ring's own loads then hit
+    // in L2.  Costs no shared memory.
+    const int pf_dist = p.prefetch_tiles;
+    auto prefetch_tile = [&](int64_t wt) {
+      if (wt >= w_end) return;
+      const Segment ps = locate(prefix, batch, hkv, total, grid, wt, w_end, p.seqlens, max_len);
+      const int pos = ps.tile0 * kTileTokens + lane * chunk;
+      if (lane < nchunks && pos < ps.seqlen) {
+        const int pg = __ldg(p.block_table + static_cast<int64_t>(ps.b) * p.bt_stride + pos / p.page);
+        const int off = pos % p.page;
+        tma_prefetch_4d(&tm_k, 0, ps.kvh, off, pg);
+        tma_prefetch_4d(&tm_k, 64, ps.kvh, off, pg);
+        tma_prefetch_4d(&tm_v, 0, ps.kvh, off, pg);
+        tma_prefetch_4d(&tm_v, 64, ps.kvh, off, pg);
+      }
+    };
+    for (int j = 1; j < pf_dist; ++j) prefetch_tile(w_begin + j);
     int64_t it = 0;
     int sc = 0;
     bool ok = true;
@@ -305,6 +357,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
           tma_load_4d(&tm_v, &full[stage], vdst, 0, s.kvh, off, page_id, pol_stream);
           tma_load_4d(&tm_v, &full[stage], vdst + kHalfBytes, 64, s.kvh, off, page_id, pol_stream);
         }
+        if (pf_dist > 0) prefetch_tile(w_begin + it + pf_dist);
         __syncwarp();
       }
       w += s.ntiles;
@@ -313,7 +366,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     // ---------------------------------------------------------- UMMA issuer
     constexpr bool kBf16 = DType<T>::kBf16;
     constexpr uint32_t idesc_qk = make_idesc(kBf16, false, false, 128, kMaxGroup);
-    constexpr uint32_t idesc_pv = make_idesc(kBf16, true, true, 128, kMaxGroup);
+    constexpr uint32_t idesc_pv = make_idesc(kBf16, true, true, 128, kPvN);
     int64_t it = 0;
     int sc = 0;
     bool ok = true;
@@ -332,9 +385,9 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
           // A = V^T: MN-major (head-dim contiguous), 128B swizzle; the two
           // 64-dim halves are 16 KB apart (LBO), 8-token groups 1 KB apart (SBO).
           const uint64_t a = make_sdesc(vaddr + j * 2048, kHalfBytes, 1024, kLayoutSw128);
-          // B = P^T: MN-major (heads contiguous), no swizzle; 8-head core
-          // matrices 128 B apart (SBO), 8-token groups 256 B apart (LBO).
-          const uint64_t b = make_sdesc(paddr + j * 512, 256, 128, kLayoutNone);
+          // B = [P_hi | P_lo]^T: MN-major (heads contiguous), no swizzle;
+          // 8-column core matrices 128 B apart (SBO), 8-token groups kPGroupBytes apart (LBO).
+          const uint64_t b = make_sdesc(paddr + j * 2 * kPGroupBytes, kPGroupBytes, 128, kLayoutNone);
           umma_f16(tmem + col_o(pb), a, b, idesc_pv, j > 0 ? 1u : 0u);
         }
         umma_commit(&o_full[pb]);
@@ -405,13 +458,14 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         const int pb = static_cast<int>(i & 1);
         mbar_wait_bounded(&o_full[pb], static_cast<uint32_t>((i >> 1) & 1), abort_flag, budget);
         tc_fence_after();
-        uint32_t r[NCOL];
-        if constexpr (NCOL == 8) tmem_ld_x8(lane_addr + col_o(pb), r); else tmem_ld_x16(lane_addr + col_o(pb), r);
+        uint32_t r[kPvN];
+        if constexpr (NCOL == 8) tmem_ld_x16(lane_addr + col_o(pb), r); else tmem_ld_x32(lane_addr + col_o(pb), r);
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&o_empty[pb]);
 #pragma unroll
-        for (int h = 0; h < NCOL; ++h) o_acc[h] = fmaf(o_acc[h], a_prev[h], __uint_as_float(r[h]));
+        for (int h = 0; h < NCOL; ++h)
+          o_acc[h] = fmaf(o_acc[h], a_prev[h], __uint_as_float(r[h]) + __uint_as_float(r[NCOL + h]));
       };
       for (int t = 0; t < s.ntiles; ++t, ++it) {
         const int sb = static_cast<int>(it & 1);
@@ -462,20 +516,17 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
           }
         }
         {
-          uint8_t* prow = pbufs + sb * kPBufBytes + (row >> 3) * 256 + (row & 7) * 16;
-          uint4 lo;
-          lo.x = DType<T>::pack2(pv[0], pv[1]);
-          lo.y = DType<T>::pack2(pv[2], pv[3]);
-          lo.z = DType<T>::pack2(pv[4], pv[5]);
-          lo.w = DType<T>::pack2(pv[6], pv[7]);
-          *reinterpret_cast<uint4*>(prow) = lo;
-          if constexpr (NCOL == 16) {
-            uint4 hi;
-            hi.x = DType<T>::pack2(pv[8], pv[9]);
-            hi.y = DType<T>::pack2(pv[10], pv[11]);
-            hi.z = DType<T>::pack2(pv[12], pv[13]);
-            hi.w = DType<T>::pack2(pv[14], pv[15]);
-            *reinterpret_cast<uint4*>(prow + 128) = hi;
+          // This token's row of [P_hi | P_lo]: 8-column chunks 128 B apart.
+          uint8_t* prow = pbufs + sb * kPBufBytes + (row >> 3) * kPGroupBytes + (row & 7) * 16;
+#pragma unroll
+          for (int c = 0; c < NCOL / 8; ++c) {
+            uint4 hi, lo;
+            DType<T>::split2(pv[8 * c + 0], pv[8 * c + 1], hi.x, lo.x);
+            DType<T>::split2(pv[8 * c + 2], pv[8 * c + 3], hi.y, lo.y);
+            DType<T>::split2(pv[8 * c + 4], pv[8 * c + 5], hi.z, lo.z);
+            DType<T>::split2(pv[8 * c + 6], pv[8 * c + 7], hi.w, lo.w);
+            *reinterpret_cast<uint4*>(prow + c * 128) = hi;
+            *reinterpret_cast<uint4*>(prow + (NCOL / 8 + c) * 128) = lo;
           }
         }
         fence_proxy_async_smem();
@@ -527,10 +578,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         named_bar_sync(1, 128);
         if (d == 0) {
           int is_last = 0;
-          if (!*abort_flag) {
-            const unsigned old = atomicInc(p.tickets + s.pair, static_cast<unsigned>(s.nseg - 1));
-            is_last = old == static_cast<unsigned>(s.nseg - 1);
-          }
+          if (!*abort_flag) is_last = ticket_arrive(p.tickets + s.pair, p.epoch, s.nseg) ? 1 : 0;
           *last_flag = is_last;
         }
         named_bar_sync(1, 128);

@@ -26,9 +26,11 @@ struct DecodeParams {
   float scale_log2;           // softmax_scale * log2(e)
   float* part_o;              // [slots, group, 128] fp32 (normalised partial O)
   float* part_lse;            // [slots, group] log2-domain partial LSE
-  uint32_t* tickets;          // [batch * num_heads_k] arrival counters, zero at rest
+  uint32_t* tickets;          // [batch * num_heads_k] epoch-tagged arrival counters
   int* err;                   // device error word
   unsigned long long timeout_ns;
+  uint32_t epoch;             // 1 .. 2^20-1, different for consecutive launches
+  int prefetch_tiles;         // L2 prefetch distance in tiles (0 = off)
 };
 
 struct SimtParams {
@@ -53,9 +55,9 @@ cudaError_t launch_decode_sm100(const CUtensorMap& tm_q, const CUtensorMap& tm_k
                                 const CUtensorMap& tm_v, const DecodeParams& p, int dtype,
                                 bool out_fp32, int grid, cudaStream_t stream);
 cudaError_t launch_decode_simt(const SimtParams& p, int dtype, bool out_fp32, cudaStream_t stream);
-cudaError_t launch_combine_lse(const float* part_o, const float* part_lse, int64_t n_parts,
-                               int64_t rows, int64_t head_dim, void* out, int out_dtype,
-                               float* lse_out, cudaStream_t stream);
+cudaError_t launch_combine_lse(const float* part_o, int64_t o_stride, const float* part_lse,
+                               int64_t l_stride, int64_t n_parts, int64_t rows, int64_t head_dim,
+                               void* out, int out_dtype, float* lse_out, cudaStream_t stream);
 
 cudaError_t launch_bounded_wait_probe(unsigned long long budget_ns, int* status,
                                       unsigned long long* waited_ns, cudaStream_t stream);

@@ -22,7 +22,7 @@ SIGNATURES: dict[str, tuple] = {
     "fd_decode_paged": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp] + [_i64] * 7
                         + [_i32, _i32, _f32, _i64, _vp, _sz, _vp]),
     "fd_decode_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
-    "fd_combine_lse": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _i32, _vp, _vp]),
+    "fd_combine_lse": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _vp, _vp]),
     "fd_last_error": (_i32, []),
     "fd_error_string": (_c.c_char_p, [_i32]),
     "fd_last_error_message": (_c.c_char_p, []),

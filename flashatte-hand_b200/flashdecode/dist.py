@@ -1,0 +1,113 @@
+"""Multi-GPU partitioning of the decode inside one node (one process per GPU).
+
+The reference has no multi-GPU code; its only decomposition is intra-GPU
+split-KV (submission-oj/best_flashattn_kvcache_decode.cu:1381-1425).  Two
+partitions are provided here:
+
+* batch sharding (``batch_shard``): each rank owns whole sequences and their
+  KV pages, chosen longest-first (LPT) so skewed length mixes balance.  No
+  collective is on the data path; every rank writes its own output rows.
+* cross-GPU split-KV (``kv_split_case`` + ``SplitKVDecode``): each rank owns
+  a contiguous page range of every sequence, decodes it to a normalised fp32
+  partial (O, LSE), and one all-gather of the packed [O | LSE] blocks
+  (B*Hq*(D+1) floats per rank) feeds the LSE combine kernel, which reads the
+  gathered buffer from local memory.  That is the reference's split/combine
+  (best :595-1037) with the splits placed on different GPUs.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as tdist
+
+from . import cases as _cases
+
+
+def batch_shard(case: _cases.DecodeCase, rank: int, world: int):
+    """(sub-case of the sequences rank owns, their global row indices)."""
+    rows = _cases.lpt_partition(case.seqlens.tolist(), world)[rank]
+    if not rows:
+        raise ValueError(f"rank {rank} of {world} owns no sequence (batch {case.B})")
+    return _cases.subset_case(case, rows, name=f"{case.name}_shard{rank}of{world}"), rows
+
+
+def kv_page_range(n_pages: int, rank: int, world: int) -> tuple[int, int]:
+    return n_pages * rank // world, n_pages * (rank + 1) // world
+
+
+def kv_split_case(case: _cases.DecodeCase, rank: int, world: int):
+    """Local view of rank's page range of every sequence.
+
+    Returns (local case with its own compact page pool, page_map) where
+    page_map[i] is the global page id of local page i.
+    """
+    page = case.page
+    sl_local, rows_pages = [], []
+    for b in range(case.B):
+        L = max(int(case.seqlens[b]), 0)
+        n = math.ceil(L / page)
+        p0, p1 = kv_page_range(n, rank, world)
+        sl_local.append(max(0, min(L, p1 * page) - p0 * page))
+        rows_pages.append(case.block_table[b, p0:p1].tolist())
+    page_map = [pg for r in rows_pages for pg in r]
+    width = max(1, max(len(r) for r in rows_pages))
+    bt = torch.full((case.B, width), -1, dtype=torch.int32)
+    off = 0
+    for b, r in enumerate(rows_pages):
+        bt[b, : len(r)] = torch.arange(off, off + len(r), dtype=torch.int32)
+        off += len(r)
+    local = _cases.DecodeCase(name=f"{case.name}_kv{rank}of{world}", dtype=case.dtype, B=case.B,
+                              Hq=case.Hq, Hkv=case.Hkv, D=case.D, page=page,
+                              seqlens=torch.tensor(sl_local, dtype=torch.int32), block_table=bt,
+                              num_blocks=max(len(page_map), 1), q_std=case.q_std,
+                              softmax_scale=case.softmax_scale)
+    return local, torch.tensor(page_map, dtype=torch.int64)
+
+
+def _default_decode(q, k, v, seqlens, bt, scale, out_o, out_lse):
+    from .ops import flash_decode
+    flash_decode(q, k, v, seqlens, bt, softmax_scale=scale, out=out_o, out_dtype=torch.float32,
+                 lse=out_lse)
+
+
+def _default_combine(part_o, part_lse, out_dtype):
+    from .ops import combine_lse
+    return combine_lse(part_o, part_lse, out_dtype=out_dtype, return_lse=True)
+
+
+class SplitKVDecode:
+    """Cross-GPU split-KV decode step: local partial -> all-gather -> combine.
+
+    ``decode_fn`` / ``combine_fn`` default to the CUDA operator; tests on CPU
+    ranks pass stand-ins to exercise the exchange protocol without a GPU.
+    """
+
+    def __init__(self, B: int, Hq: int, D: int, out_dtype: torch.dtype, device,
+                 group=None, decode_fn=None, combine_fn=None):
+        self.B, self.Hq, self.D = B, Hq, D
+        self.rows = B * Hq
+        self.block = self.rows * D + self.rows
+        self.group = group
+        self.world = tdist.get_world_size(group)
+        self.out_dtype = out_dtype
+        self.send = torch.empty(self.block, dtype=torch.float32, device=device)
+        self.recv = torch.empty(self.world * self.block, dtype=torch.float32, device=device)
+        self.decode_fn = decode_fn or _default_decode
+        self.combine_fn = combine_fn or _default_combine
+        self._flat = tdist.get_backend(group) == "nccl"
+
+    def __call__(self, q, k_local, v_local, seqlens_local, bt_local, softmax_scale: float):
+        o_view = self.send[: self.rows * self.D].view(self.B, 1, self.Hq, self.D)
+        l_view = self.send[self.rows * self.D:].view(self.B, self.Hq)
+        self.decode_fn(q, k_local, v_local, seqlens_local, bt_local, softmax_scale, o_view, l_view)
+        if self._flat:
+            tdist.all_gather_into_tensor(self.recv, self.send, group=self.group)
+        else:
+            tdist.all_gather(list(self.recv.view(self.world, self.block).unbind(0)), self.send,
+                             group=self.group)
+        parts = self.recv.view(self.world, self.block)
+        part_o = parts[:, : self.rows * self.D].view(self.world, self.rows, self.D)
+        part_l = parts[:, self.rows * self.D:]
+        out, lse = self.combine_fn(part_o, part_l, self.out_dtype)
+        return out.view(self.B, 1, self.Hq, self.D), lse.view(self.B, self.Hq)

@@ -66,12 +66,14 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                  softmax_scale: float | None = None, return_softmax_lse: bool = False,
                  out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
                  max_seqlen_k: int | None = None, workspace: torch.Tensor | None = None,
-                 stream: torch.cuda.Stream | None = None):
+                 stream: torch.cuda.Stream | None = None, lse: torch.Tensor | None = None):
     """Single-token paged decode attention.
 
     q [B, 1, Hq, D]; k_cache/v_cache [num_blocks, page, Hkv, D];
     cache_seqlens [B] int32; block_table [B, max_blocks] int32.
-    Returns out [B, 1, Hq, D] (and lse [B, Hq] fp32, natural log).
+    Returns out [B, 1, Hq, D] (and lse [B, Hq] fp32, natural log).  `out` and
+    `lse` may be given as preallocated contiguous buffers; passing `lse`
+    implies return_softmax_lse.
     """
     lib = load_library()
     _require_cuda(q, k_cache, v_cache, cache_seqlens, block_table)
@@ -97,7 +99,12 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
         out = torch.empty((B, 1, Hq, D), dtype=odt, device=q.device)
     elif out.dtype != odt or tuple(out.shape) != (B, 1, Hq, D) or not out.is_contiguous():
         raise ValueError("out has the wrong shape, dtype or layout")
-    lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device) if return_softmax_lse else None
+    if lse is not None:
+        if lse.dtype != torch.float32 or tuple(lse.shape) != (B, Hq) or not lse.is_contiguous():
+            raise ValueError("lse must be a contiguous fp32 [B, Hq] tensor")
+        return_softmax_lse = True
+    elif return_softmax_lse:
+        lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
     ws_ptr, ws_bytes = None, 0
     if workspace is not None:
         ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
@@ -117,21 +124,26 @@ def combine_lse(part_o: torch.Tensor, part_lse: torch.Tensor, out_dtype: torch.d
     """Merge partial results over disjoint KV ranges.
 
     part_o [n, rows, D] fp32 (normalised), part_lse [n, rows] fp32 natural log.
+    Each part must be contiguous; the parts themselves may be strided (views
+    into one gathered buffer of per-part [O | LSE] blocks).
     Returns out [rows, D] (and lse [rows]).
     """
     lib = load_library()
     _require_cuda(part_o, part_lse)
     if part_o.dtype != torch.float32 or part_lse.dtype != torch.float32:
         raise ValueError("partials must be fp32")
-    part_o = part_o.contiguous()
-    part_lse = part_lse.contiguous()
     n, rows, D = part_o.shape
+    if part_o.stride()[1:] != (D, 1):
+        part_o = part_o.contiguous()
+    if part_lse.stride(1) != 1:
+        part_lse = part_lse.contiguous()
     out = torch.empty((rows, D), dtype=out_dtype, device=part_o.device)
     lse = torch.empty((rows,), dtype=torch.float32, device=part_o.device) if return_lse else None
     st = stream if stream is not None else torch.cuda.current_stream(part_o.device)
     with torch.cuda.device(part_o.device):
-        status = lib.fd_combine_lse(_ptr(part_o), _ptr(part_lse), n, rows, D, _ptr(out),
-                                    _OUT_DTYPES[out_dtype], _ptr(lse), st.cuda_stream)
+        status = lib.fd_combine_lse(_ptr(part_o), part_o.stride(0), _ptr(part_lse), part_lse.stride(0),
+                                    n, rows, D, _ptr(out), _OUT_DTYPES[out_dtype], _ptr(lse),
+                                    st.cuda_stream)
     check(status)
     return (out, lse) if return_lse else out
 

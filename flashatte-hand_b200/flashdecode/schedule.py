@@ -54,6 +54,7 @@ def segments(seqlens, hkv: int, grid: int, max_len: int | None = None) -> list[S
     for x in n:
         prefix.append(prefix[-1] + x)
     total = hkv * prefix[-1]
+    grid = min(grid, total)  # the kernel never splits over more CTAs than tiles
     out: list[Segment] = []
     for c in range(grid):
         w, w_end = total * c // grid, total * (c + 1) // grid

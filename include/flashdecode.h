@@ -76,8 +76,8 @@ void run_kernel(const void* q, const void* k_cache_paged, const void* v_cache_pa
  * out_dtype:    FD_DTYPE_FP32 or the value of dtype.
  * max_seqlen_k: upper bound on cache_seqlens (0 = unknown); only sizes the grid.
  * workspace:    device buffer of at least fd_decode_workspace_size(...) bytes,
- *               zero-filled before its first use (the operator leaves it
- *               zeroed after every successful call), or NULL to use a
+ *               any contents (it needs no clearing: counters in it are
+ *               tagged with a per-launch epoch), or NULL to use a
  *               library-owned per-device buffer.  One workspace must not be
  *               used by two calls that can run at the same time.
  * stream:       cudaStream_t (NULL = legacy default stream).
@@ -102,15 +102,20 @@ size_t fd_decode_workspace_size(int64_t batch_size, int64_t num_heads, int64_t n
 /*
  * fd_combine_lse - merge n_parts partial attention results computed over
  * disjoint KV ranges into one (the cross-GPU split-KV exchange step).
- * part_o   [n_parts, rows, headdim] fp32, each part already normalised;
- * part_lse [n_parts, rows] fp32 natural log (-inf = empty part);
+ * part_o   part j at part_o + j * part_o_stride: [rows, headdim] fp32, each
+ *          part already normalised (part_o_stride 0 = rows * headdim);
+ * part_lse part j at part_lse + j * part_lse_stride: [rows] fp32 natural
+ *          log, -inf = empty part (part_lse_stride 0 = rows);
  * out      [rows, headdim] of out_dtype; lse_out [rows] (nullable).
+ * The strides let one gathered buffer of per-part [O | LSE] blocks be merged
+ * in place.
  * Replaces: combine_split_lse_kernel (best :956-1037) and combine_lse_kernel
  * _v11 (v11_best_hybrid/..._v11_best_hybrid.cu:574-614), including the rule
  * that empty parts get weight zero.
  */
-int fd_combine_lse(const float* part_o, const float* part_lse, int64_t n_parts, int64_t rows,
-                   int64_t headdim, void* out, int out_dtype, float* lse_out, void* stream);
+int fd_combine_lse(const float* part_o, int64_t part_o_stride, const float* part_lse,
+                   int64_t part_lse_stride, int64_t n_parts, int64_t rows, int64_t headdim,
+                   void* out, int out_dtype, float* lse_out, void* stream);
 
 /* Status of the last call made on this host thread, and its message. */
 int fd_last_error(void);

@@ -1,0 +1,109 @@
+"""CPU checks of the host-side logic: workload layouts and the split scheduler
+model (the same partition the kernel computes on the device)."""
+import math
+
+import pytest
+import torch
+
+from flashdecode import cases, schedule
+
+
+def test_config2_matches_baseline_sizes():
+    c = cases.config_case(2)
+    assert (c.B, c.Hq, c.Hkv, c.D, c.page, c.dtype) == (64, 32, 8, 128, 256, torch.bfloat16)
+    assert torch.all(c.seqlens == 4096)
+    assert c.num_blocks == 1024
+    assert sorted(c.block_table.flatten().tolist()) == list(range(1024))
+    assert c.kv_bytes() == 1_073_741_824
+    assert c.algorithmic_bytes() == 1_074_802_944
+    assert c.flops() == 4 * 64 * 4096 * 32 * 128
+
+
+@pytest.mark.parametrize("idx", [1, 3, 5])
+def test_random_layouts_use_every_page_once(idx):
+    c = cases.config_case(idx)
+    used = c.block_table[c.block_table >= 0]
+    assert used.numel() == c.num_blocks
+    assert torch.equal(used.sort().values, torch.arange(c.num_blocks, dtype=torch.int32))
+    n = (c.seqlens + c.page - 1) // c.page
+    for b in range(c.B):
+        assert torch.all(c.block_table[b, : n[b]] >= 0)
+        assert torch.all(c.block_table[b, n[b]:] == -1)
+
+
+def test_length_distributions():
+    c1, c3, c5 = cases.config_case(1), cases.config_case(3), cases.config_case(5)
+    assert c1.seqlens.min() >= 1 and c1.seqlens.max() <= 2048
+    assert c3.seqlens.min() >= 16 and c3.seqlens.max() <= 32768
+    assert c3.seqlens.float().log().std() > 1.0  # log-uniform spread
+    assert c5.seqlens.min() >= 512 and c5.seqlens.max() <= 8192
+    assert (c5.Hq, c5.Hkv, c5.page, c5.dtype) == (28, 4, 16, torch.float16)
+    c4 = cases.config_case(4)
+    assert c4.kv_bytes() == 2_147_483_648 and c4.q_std == 0.5
+
+
+def test_contest_layout_formula():
+    c = cases.contest_case(16, 141, 4)
+    assert c.num_blocks == 16 * math.ceil(141 / 16)
+    assert c.block_table.shape == (16, 9)
+    assert c.seqlens[0] == 141 and c.seqlens[1] == 1
+    assert c.seqlens[5] == 1 + ((5 * 9973 + 141 // 3) % 140)
+
+
+def test_materialize_is_deterministic_on_cpu():
+    c = cases.custom_case("det", torch.bfloat16, [10, 3], 8, 2, page=16)
+    a, b = cases.materialize(c, "cpu", seed=3), cases.materialize(c, "cpu", seed=3)
+    assert all(torch.equal(a[k], b[k]) for k in a)
+
+
+def test_subset_case_compacts_pool():
+    c = cases.config_case(3)
+    rows = [5, 17, 100]
+    s = cases.subset_case(c, rows)
+    assert s.B == 3 and torch.equal(s.seqlens, c.seqlens[rows])
+    assert s.num_blocks == int(((c.seqlens[rows] + 255) // 256).sum())
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_lpt_partition_balances_skew(world):
+    c = cases.config_case(3)
+    shards = cases.lpt_partition(c.seqlens.tolist(), world)
+    assert sorted(sum(shards, [])) == list(range(c.B))
+    loads = [int(c.seqlens[s].sum()) for s in shards]
+    assert max(loads) - min(loads) <= int(c.seqlens.max())
+
+
+@pytest.mark.parametrize("seqlens,hkv,grid", [
+    ([4096] * 64, 8, 148), ([1, 0, 5000, 300, 128, 129], 4, 148), ([262144] * 2, 8, 148),
+    ([0], 1, 1), ([7, 9], 2, 3), (list(range(0, 3000, 37)), 8, 148),
+    ([300, 7], 8, 148), ([1, 127, 128, 129, 300, 0, 1000, 2049], 4, 148),
+    ([1, 127, 128, 129, 300, 0, 1000, 2049], 1, 148),
+])
+def test_schedule_covers_every_tile_once(seqlens, hkv, grid):
+    segs = schedule.segments(seqlens, hkv, grid)
+    seen = {}
+    for s in segs:
+        for t in range(s.tile0, s.tile0 + s.ntiles):
+            key = (s.pair, t)
+            assert key not in seen
+            seen[key] = s.cta
+    want = {(b * hkv + h, t) for b, L in enumerate(seqlens) for h in range(hkv)
+            for t in range(schedule.tiles_of(L))}
+    assert set(seen) == want
+    # partial slots c + pair are unique and below grid + pairs
+    slots = [s.slot for s in segs if s.nseg > 1]
+    assert len(slots) == len(set(slots))
+    assert all(0 <= x < grid + len(seqlens) * hkv for x in slots)
+    # segment count of a pair equals its nseg, and they are numbered from cfirst
+    by_pair = {}
+    for s in segs:
+        by_pair.setdefault(s.pair, []).append(s)
+    for pair, ss in by_pair.items():
+        assert len(ss) == ss[0].nseg
+        assert [s.cta for s in ss] == list(range(ss[0].cfirst, ss[0].cfirst + ss[0].nseg))
+
+
+def test_schedule_is_balanced_on_config2():
+    st = schedule.split_stats([4096] * 64, 8, 148)
+    assert st["tiles_total"] == 64 * 8 * 32
+    assert st["tiles_per_cta_max"] - st["tiles_per_cta_min"] <= 1
