@@ -220,7 +220,7 @@ def main():
                                  t["block_table"], softmax_scale=case.softmax_scale,
                                  return_softmax_lse=True, max_seqlen_k=int(case.seqlens.max()))
 
-    launches_per_call = math.ceil(case.B / 2048)
+    launches_per_call = math.ceil(case.B / 1024)
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()

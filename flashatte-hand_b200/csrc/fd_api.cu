@@ -26,7 +26,6 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 constexpr unsigned long long kDefaultTimeoutNs = 1000000000ull;  // 1 s per in-kernel wait
-constexpr int kDefaultPrefetchTiles = 4;
 
 thread_local int t_last_error = FD_OK;
 thread_local char t_last_msg[256] = "ok";
@@ -112,11 +111,16 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int esize(int dtype) { return dtype == FD_DTYPE_FP32 ? 4 : 2; }
 
+// Tokens per TMA box for full tiles: the largest of 128/64/32/16 dividing the
+// page (a box never crosses a page).  FD_TMA_CHUNK lowers it (tuning aid).
 int pick_chunk(int64_t page) {
-  if (page % 128 == 0) return 128;
-  if (page % 64 == 0) return 64;
-  if (page % 32 == 0) return 32;
-  if (page % 16 == 0) return 16;
+  static const int cap = [] {
+    const char* e = std::getenv("FD_TMA_CHUNK");
+    const int v = e != nullptr ? std::atoi(e) : 128;
+    return (v == 16 || v == 32 || v == 64) ? v : 128;
+  }();
+  for (int c = cap; c >= 16; c /= 2)
+    if (page % c == 0) return c;
   return 0;
 }
 
@@ -137,20 +141,6 @@ CUresult encode(CUtensorMap* m, int dtype, int rank, const void* base, const cuu
 uint32_t next_epoch() {
   static std::atomic<uint32_t> counter{0};
   return counter.fetch_add(1, std::memory_order_relaxed) % 0xFFFFFu + 1u;
-}
-
-// L2 prefetch distance of the tensor-core kernel, in 128-token tiles
-// (FD_PREFETCH_TILES overrides; 0 disables).
-int prefetch_tiles() {
-  static int v = [] {
-    const char* e = std::getenv("FD_PREFETCH_TILES");
-    if (e != nullptr) {
-      const long x = std::strtol(e, nullptr, 10);
-      if (x >= 0 && x <= 64) return static_cast<int>(x);
-    }
-    return kDefaultPrefetchTiles;
-  }();
-  return v;
 }
 
 unsigned long long timeout_ns() {
@@ -283,28 +273,30 @@ int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, voi
       max_seqlen_k > 0 ? (max_seqlen_k < kv_max ? max_seqlen_k : kv_max) : kv_max;
   const int64_t tiles_bound = len_bound > 0 ? (len_bound + fd::kTileTokens - 1) / fd::kTileTokens : 1;
 
-  CUtensorMap tm_k, tm_v;
+  fd::TensorMaps maps;
   {
     const cuuint64_t dims[4] = {128, (cuuint64_t)num_heads_k, (cuuint64_t)page_block_size,
                                 (cuuint64_t)num_blocks};
     const cuuint64_t strides[3] = {(cuuint64_t)(128 * es), (cuuint64_t)(num_heads_k * 128 * es),
                                    (cuuint64_t)(page_block_size * num_heads_k * 128 * es)};
     const cuuint32_t box[4] = {64, 1, (cuuint32_t)chunk, 1};
-    CUresult r = encode(&tm_k, dtype, 4, k_cache, dims, strides, box);
-    if (r == CUDA_SUCCESS) r = encode(&tm_v, dtype, 4, v_cache, dims, strides, box);
+    const cuuint32_t box16[4] = {64, 1, 16, 1};
+    CUresult r = encode(&maps.k, dtype, 4, k_cache, dims, strides, box);
+    if (r == CUDA_SUCCESS) r = encode(&maps.v, dtype, 4, v_cache, dims, strides, box);
+    if (r == CUDA_SUCCESS) r = encode(&maps.k16, dtype, 4, k_cache, dims, strides, box16);
+    if (r == CUDA_SUCCESS) r = encode(&maps.v16, dtype, 4, v_cache, dims, strides, box16);
     if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "K/V tensor map encode failed (%d)", (int)r);
   }
 
   for (int64_t b0 = 0; b0 < batch_size; b0 += fd::kMaxBatchPerLaunch) {
     const int64_t nb = batch_size - b0 < fd::kMaxBatchPerLaunch ? batch_size - b0
                                                                  : fd::kMaxBatchPerLaunch;
-    CUtensorMap tm_q;
     {
       const uint8_t* qb = static_cast<const uint8_t*>(q) + b0 * num_heads * 128 * es;
       const cuuint64_t dims[3] = {128, (cuuint64_t)num_heads, (cuuint64_t)nb};
       const cuuint64_t strides[2] = {(cuuint64_t)(128 * es), (cuuint64_t)(num_heads * 128 * es)};
       const cuuint32_t box[3] = {64, (cuuint32_t)group, 1};
-      const CUresult r = encode(&tm_q, dtype, 3, qb, dims, strides, box);
+      const CUresult r = encode(&maps.q, dtype, 3, qb, dims, strides, box);
       if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "Q tensor map encode failed (%d)", (int)r);
     }
     fd::DecodeParams p;
@@ -326,10 +318,9 @@ int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, voi
     p.part_o = reinterpret_cast<float*>(ws + wl.o_off);
     p.timeout_ns = timeout_ns();
     p.epoch = next_epoch();
-    p.prefetch_tiles = prefetch_tiles();
     const int64_t work_bound = nb * num_heads_k * tiles_bound;
     const int grid = static_cast<int>(work_bound < sms ? work_bound : sms);
-    const cudaError_t e = fd::launch_decode_sm100(tm_q, tm_k, tm_v, p, dtype, out_fp32, grid, st);
+    const cudaError_t e = fd::launch_decode_sm100(maps, p, dtype, out_fp32, grid, st);
     if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "sm100 launch: %s", cudaGetErrorString(e));
   }
   return set_ok();

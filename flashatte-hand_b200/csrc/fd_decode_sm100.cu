@@ -15,10 +15,13 @@
 // Per tile the CTA runs, warp-specialised:
 //   warp 0    TMA producer: gathers the tile's K and V rows page by page
 //             through block_table into a 3-deep shared-memory ring
-//             (128B-swizzled, two 64-dim halves), and the group's query rows.
+//             (128B-swizzled, two 64-dim halves), with the group's query rows
+//             riding in the same stage; a sequence's last, partial tile is
+//             fetched in 16-token boxes covering only its valid rows.
 //   warp 1    tcgen05 issuer: S^T[tok, head] = K . Q^T (M=128 tokens, N=16
 //             heads, K=128 dims) into TMEM, then O^T[dim, head] = V^T . P^T
-//             (M=128 dims, N=16 heads, K=128 tokens) into TMEM.
+//             (M=128 dims, N=2x16 heads, K=128 tokens) into TMEM, each issued
+//             as soon as its inputs are ready (no fixed QK/PV interleave).
 //   warps 2-5 softmax + epilogue: thread = TMEM lane = token row for S and
 //             head-dim for O; fp32 online softmax in the log2 domain (the
 //             reference's convention, best :541-578), P written to shared
@@ -38,19 +41,18 @@ namespace {
 constexpr int kStages = 3;
 constexpr int kHalfBytes = kTileTokens * 128;    // 128 tokens x 64 dims x 2 B = 16 KB
 constexpr int kOperandBytes = 2 * kHalfBytes;    // one K or V tile: 32 KB
-constexpr int kStageBytes = 2 * kOperandBytes;   // K + V: 64 KB
 constexpr int kQSlotBytes = 2 * kMaxGroup * 128; // two halves x 16 rows x 128 B
+constexpr int kStageBytes = 2 * kOperandBytes + kQSlotBytes;  // K + V + Q: 68 KB
 // P is stored as two 16-bit parts, P = hi + lo (hi = round(P), lo = round(P - hi)),
 // side by side in the UMMA N dimension: 128 tokens x (2 x 16 heads) x 2 B.
 // Summing V.hi and V.lo keeps P's fp32 precision through a 16-bit MMA.
 constexpr int kPBufBytes = kTileTokens * 2 * kMaxGroup * 2;
 constexpr int kTmemCols = 128;                   // S0 S1 (16 cols each), O0 O1 (32 each)
-constexpr int kNumBars = 2 * kStages + 14;
+constexpr int kNumBars = 2 * kStages + 10;
 
 // Shared-memory carve-up, offsets from a 1024-byte aligned base.
 constexpr int kOffStages = 0;
-constexpr int kOffQ = kOffStages + kStages * kStageBytes;
-constexpr int kOffP = kOffQ + 2 * kQSlotBytes;
+constexpr int kOffP = kOffStages + kStages * kStageBytes;
 constexpr int kOffBars = kOffP + 2 * kPBufBytes;
 constexpr int kOffMisc = kOffBars + kNumBars * 8;            // tmem slot, abort, last flag
 constexpr int kOffRed = (kOffMisc + 64 + 15) & ~15;          // [2][4][16] floats tile maxima
@@ -188,7 +190,9 @@ template <typename T, typename OutT, int NCOL>
 __global__ void __launch_bounds__(kSm100Threads, 1)
     decode_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
-                        const __grid_constant__ CUtensorMap tm_v, const DecodeParams p) {
+                        const __grid_constant__ CUtensorMap tm_v,
+                        const __grid_constant__ CUtensorMap tm_k16,
+                        const __grid_constant__ CUtensorMap tm_v16, const DecodeParams p) {
   // P.V uses N = 2*NCOL columns: NCOL hi parts then NCOL lo parts of P.
   constexpr int kPvN = 2 * NCOL;
   constexpr int kPGroupBytes = (kPvN / 8) * 128;  // one 8-token group of P rows
@@ -196,15 +200,13 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
 
+  // Stage s: K tile at +0, V tile at +32 KB, query rows at +64 KB.
   uint8_t* stages = smem + kOffStages;
-  uint8_t* qslots = smem + kOffQ;
   uint8_t* pbufs = smem + kOffP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
   uint64_t* full = bars;
   uint64_t* empty = bars + kStages;
-  uint64_t* q_full = bars + 2 * kStages;
-  uint64_t* q_empty = q_full + 2;
-  uint64_t* s_full = q_empty + 2;
+  uint64_t* s_full = bars + 2 * kStages;
   uint64_t* s_empty = s_full + 2;
   uint64_t* p_full = s_empty + 2;
   uint64_t* o_full = p_full + 2;
@@ -232,8 +234,6 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 128);
       mbar_init(&p_full[i], 128);
@@ -245,12 +245,15 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
-  // Zero the query slots (rows >= group stay zero) and the P buffers
-  // (heads >= group stay zero): 16 KB.
+  // Zero the stages' query areas (rows >= group stay zero: the query TMA
+  // writes rows < group only) and the P buffers (heads >= group stay zero).
+  for (int s = 0; s < kStages; ++s) {
+    uint4* z = reinterpret_cast<uint4*>(stages + s * kStageBytes + 2 * kOperandBytes);
+    for (int i = tid; i < kQSlotBytes / 16; i += kSm100Threads) z[i] = make_uint4(0, 0, 0, 0);
+  }
   {
-    uint4* z = reinterpret_cast<uint4*>(qslots);
-    const int n16 = (2 * kQSlotBytes + 2 * kPBufBytes) / 16;
-    for (int i = tid; i < n16; i += kSm100Threads) z[i] = make_uint4(0, 0, 0, 0);
+    uint4* z = reinterpret_cast<uint4*>(pbufs);
+    for (int i = tid; i < 2 * kPBufBytes / 16; i += kSm100Threads) z[i] = make_uint4(0, 0, 0, 0);
   }
   for (int b = tid; b < batch; b += kSm100Threads) {
     int len = __ldg(p.seqlens + b);
@@ -296,123 +299,123 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_k16);
+      tma_prefetch_desc(&tm_v16);
     }
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_keep = policy_evict_last();
-    const int chunk = p.chunk;  // tokens per TMA box; never crosses a page
+    const int chunk = p.chunk;  // tokens per TMA box of a full tile; never crosses a page
     const int nchunks = kTileTokens / chunk;
-    // L2 prefetch of the tile `pf_dist` tiles past the one being loaded into
-    // shared memory: the DRAM requests for upcoming tiles are in flight while
-    // the shared-memory ring is still full, and the ring's own loads then hit
-    // in L2.  Costs no shared memory.
-    const int pf_dist = p.prefetch_tiles;
-    auto prefetch_tile = [&](int64_t wt) {
-      if (wt >= w_end) return;
-      const Segment ps = locate(prefix, batch, hkv, total, grid, wt, w_end, p.seqlens, max_len);
-      const int pos = ps.tile0 * kTileTokens + lane * chunk;
-      if (lane < nchunks && pos < ps.seqlen) {
-        const int pg = __ldg(p.block_table + static_cast<int64_t>(ps.b) * p.bt_stride + pos / p.page);
-        const int off = pos % p.page;
-        tma_prefetch_4d(&tm_k, 0, ps.kvh, off, pg);
-        tma_prefetch_4d(&tm_k, 64, ps.kvh, off, pg);
-        tma_prefetch_4d(&tm_v, 0, ps.kvh, off, pg);
-        tma_prefetch_4d(&tm_v, 64, ps.kvh, off, pg);
-      }
-    };
-    for (int j = 1; j < pf_dist; ++j) prefetch_tile(w_begin + j);
     int64_t it = 0;
-    int sc = 0;
     bool ok = true;
-    for (int64_t w = w_begin; w < w_end && ok; ++sc) {
+    for (int64_t w = w_begin; w < w_end && ok;) {
       const Segment s = locate(prefix, batch, hkv, total, grid, w, w_end, p.seqlens, max_len);
-      const int qs = sc & 1;
-      ok = lane0_wait(&q_empty[qs], ((sc >> 1) & 1) ^ 1, abort_flag, budget, lane);
-      if (!ok) break;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&q_full[qs], 2u * group * 128u);
-        uint8_t* dst = qslots + qs * kQSlotBytes;
-        tma_load_3d(&tm_q, &q_full[qs], dst, 0, s.kvh * group, s.b, pol_keep);
-        tma_load_3d(&tm_q, &q_full[qs], dst + kQSlotBytes / 2, 64, s.kvh * group, s.b, pol_keep);
-      }
       const int32_t* bt_row = p.block_table + static_cast<int64_t>(s.b) * p.bt_stride;
       for (int t = 0; t < s.ntiles; ++t, ++it) {
         const int tok0 = (s.tile0 + t) * kTileTokens;
-        const int pos = tok0 + lane * chunk;
-        const bool need = lane < nchunks && pos < s.seqlen;
+        const int valid_rows = s.seqlen - tok0;
+        // Full tile: `nchunks` boxes of `chunk` tokens.  Last partial tile:
+        // 16-token boxes over the valid rows only.
+        const bool tail = valid_rows < kTileTokens;
+        const int box = tail ? 16 : chunk;
+        const int nbox = tail ? (valid_rows > 0 ? (valid_rows + 15) / 16 : 0) : nchunks;
+        const int pos = tok0 + lane * box;
+        const bool need = lane < nbox;
         int page_id = 0;
         if (need) page_id = __ldg(bt_row + pos / p.page);  // issued before the wait
-        const uint32_t nneed = __popc(__ballot_sync(0xffffffffu, need));
         const int stage = static_cast<int>(it % kStages);
         ok = lane0_wait(&empty[stage], static_cast<uint32_t>((it / kStages) & 1) ^ 1u, abort_flag,
                         budget, lane);
         if (!ok) break;
-        if (lane == 0) mbar_arrive_expect_tx(&full[stage], nneed * static_cast<uint32_t>(chunk) * 512u);
+        uint8_t* kdst = stages + stage * kStageBytes;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(nbox * box) * 512u + 2u * group * 128u);
+          uint8_t* qdst = kdst + 2 * kOperandBytes;
+          tma_load_3d(&tm_q, &full[stage], qdst, 0, s.kvh * group, s.b, pol_keep);
+          tma_load_3d(&tm_q, &full[stage], qdst + kQSlotBytes / 2, 64, s.kvh * group, s.b, pol_keep);
+        }
         __syncwarp();
         if (need) {
           const int off = pos % p.page;
-          uint8_t* kdst = stages + stage * kStageBytes + lane * chunk * 128;
-          uint8_t* vdst = kdst + kOperandBytes;
-          tma_load_4d(&tm_k, &full[stage], kdst, 0, s.kvh, off, page_id, pol_stream);
-          tma_load_4d(&tm_k, &full[stage], kdst + kHalfBytes, 64, s.kvh, off, page_id, pol_stream);
-          tma_load_4d(&tm_v, &full[stage], vdst, 0, s.kvh, off, page_id, pol_stream);
-          tma_load_4d(&tm_v, &full[stage], vdst + kHalfBytes, 64, s.kvh, off, page_id, pol_stream);
+          const CUtensorMap* mk = tail ? &tm_k16 : &tm_k;
+          const CUtensorMap* mv = tail ? &tm_v16 : &tm_v;
+          uint8_t* kd = kdst + lane * box * 128;
+          uint8_t* vd = kd + kOperandBytes;
+          tma_load_4d(mk, &full[stage], kd, 0, s.kvh, off, page_id, pol_stream);
+          tma_load_4d(mk, &full[stage], kd + kHalfBytes, 64, s.kvh, off, page_id, pol_stream);
+          tma_load_4d(mv, &full[stage], vd, 0, s.kvh, off, page_id, pol_stream);
+          tma_load_4d(mv, &full[stage], vd + kHalfBytes, 64, s.kvh, off, page_id, pol_stream);
         }
-        if (pf_dist > 0) prefetch_tile(w_begin + it + pf_dist);
         __syncwarp();
       }
       w += s.ntiles;
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- UMMA issuer
+    // Tiles 0 .. ntiles-1 of this CTA's range.  QK(i) needs stage i loaded
+    // and S buffer i%2 drained; PV(i) needs P(i) written and O buffer i%2
+    // drained.  Whichever is ready is issued (PV first: it frees a stage).
     constexpr bool kBf16 = DType<T>::kBf16;
     constexpr uint32_t idesc_qk = make_idesc(kBf16, false, false, 128, kMaxGroup);
     constexpr uint32_t idesc_pv = make_idesc(kBf16, true, true, 128, kPvN);
-    int64_t it = 0;
-    int sc = 0;
-    bool ok = true;
-    auto issue_pv = [&](int64_t i) -> bool {
-      const int pb = static_cast<int>(i & 1);
-      const uint32_t ph = static_cast<uint32_t>((i >> 1) & 1);
-      const int stage = static_cast<int>(i % kStages);
-      if (!lane0_wait(&p_full[pb], ph, abort_flag, budget, lane)) return false;
-      if (!lane0_wait(&o_empty[pb], ph ^ 1u, abort_flag, budget, lane)) return false;
+    const int64_t ntiles = w_end - w_begin;
+    int64_t qk = 0, pv = 0;
+    uint64_t idle_since = 0;
+    uint32_t spins = 0;
+    while (pv < ntiles) {
+      int action = 0;  // 1 = PV, 2 = QK
+      if (lane == 0) {
+        if (pv < qk) {
+          const int pb = static_cast<int>(pv & 1);
+          const uint32_t ph = static_cast<uint32_t>((pv >> 1) & 1);
+          if (mbar_test_wait(&p_full[pb], ph) && mbar_test_wait(&o_empty[pb], ph ^ 1u)) action = 1;
+        }
+        if (action == 0 && qk < ntiles) {
+          const int st = static_cast<int>(qk % kStages);
+          if (mbar_test_wait(&full[st], static_cast<uint32_t>((qk / kStages) & 1)) &&
+              mbar_test_wait(&s_empty[qk & 1], static_cast<uint32_t>(((qk >> 1) & 1) ^ 1)))
+            action = 2;
+        }
+        if (action == 0) {
+          if (((++spins) & 255u) == 0u) {
+            const uint64_t now = globaltimer_ns();
+            if (idle_since == 0) idle_since = now;
+            if (*abort_flag || now - idle_since > budget) {
+              *abort_flag = 1;
+              action = 3;
+            }
+          }
+        } else {
+          idle_since = 0;
+        }
+      }
+      action = __shfl_sync(0xffffffffu, action, 0);
+      if (action == 3) break;
+      if (action == 0) continue;
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t vaddr = smem_u32(stages + stage * kStageBytes + kOperandBytes);
-        const uint32_t paddr = smem_u32(pbufs + pb * kPBufBytes);
+        if (action == 1) {
+          const int pb = static_cast<int>(pv & 1);
+          const int stage = static_cast<int>(pv % kStages);
+          const uint32_t vaddr = smem_u32(stages + stage * kStageBytes + kOperandBytes);
+          const uint32_t paddr = smem_u32(pbufs + pb * kPBufBytes);
 #pragma unroll
-        for (int j = 0; j < kTileTokens / 16; ++j) {
-          // A = V^T: MN-major (head-dim contiguous), 128B swizzle; the two
-          // 64-dim halves are 16 KB apart (LBO), 8-token groups 1 KB apart (SBO).
-          const uint64_t a = make_sdesc(vaddr + j * 2048, kHalfBytes, 1024, kLayoutSw128);
-          // B = [P_hi | P_lo]^T: MN-major (heads contiguous), no swizzle;
-          // 8-column core matrices 128 B apart (SBO), 8-token groups kPGroupBytes apart (LBO).
-          const uint64_t b = make_sdesc(paddr + j * 2 * kPGroupBytes, kPGroupBytes, 128, kLayoutNone);
-          umma_f16(tmem + col_o(pb), a, b, idesc_pv, j > 0 ? 1u : 0u);
-        }
-        umma_commit(&o_full[pb]);
-        umma_commit(&empty[stage]);
-      }
-      __syncwarp();
-      return true;
-    };
-    for (int64_t w = w_begin; w < w_end && ok; ++sc) {
-      const Segment s = locate(prefix, batch, hkv, total, grid, w, w_end, p.seqlens, max_len);
-      const int qs = sc & 1;
-      ok = lane0_wait(&q_full[qs], (sc >> 1) & 1, abort_flag, budget, lane);
-      if (!ok) break;
-      for (int t = 0; t < s.ntiles; ++t, ++it) {
-        const int stage = static_cast<int>(it % kStages);
-        const int sb = static_cast<int>(it & 1);
-        ok = lane0_wait(&full[stage], static_cast<uint32_t>((it / kStages) & 1), abort_flag, budget,
-                        lane);
-        if (ok) ok = lane0_wait(&s_empty[sb], static_cast<uint32_t>(((it >> 1) & 1) ^ 1), abort_flag,
-                                budget, lane);
-        if (!ok) break;
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t kaddr = smem_u32(stages + stage * kStageBytes);
-          const uint32_t qaddr = smem_u32(qslots + qs * kQSlotBytes);
+          for (int j = 0; j < kTileTokens / 16; ++j) {
+            // A = V^T: MN-major (head-dim contiguous), 128B swizzle; the two
+            // 64-dim halves are 16 KB apart (LBO), 8-token groups 1 KB apart (SBO).
+            const uint64_t a = make_sdesc(vaddr + j * 2048, kHalfBytes, 1024, kLayoutSw128);
+            // B = [P_hi | P_lo]^T: MN-major (heads contiguous), no swizzle;
+            // 8-column core matrices 128 B apart (SBO), 8-token groups kPGroupBytes apart (LBO).
+            const uint64_t b = make_sdesc(paddr + j * 2 * kPGroupBytes, kPGroupBytes, 128, kLayoutNone);
+            umma_f16(tmem + col_o(pb), a, b, idesc_pv, j > 0 ? 1u : 0u);
+          }
+          umma_commit(&o_full[pb]);
+          umma_commit(&empty[stage]);
+        } else {
+          const int st = static_cast<int>(qk % kStages);
+          const int sb = static_cast<int>(qk & 1);
+          const uint32_t kaddr = smem_u32(stages + st * kStageBytes);
+          const uint32_t qaddr = kaddr + 2 * kOperandBytes;
 #pragma unroll
           for (int j = 0; j < kHeadDim / 16; ++j) {
             // A = K tile, K-major 128B swizzle: 8-row groups 1 KB apart; the
@@ -424,17 +427,11 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
             umma_f16(tmem + col_s(sb), a, b, idesc_qk, j > 0 ? 1u : 0u);
           }
           umma_commit(&s_full[sb]);
-          if (t == s.ntiles - 1) umma_commit(&q_empty[qs]);
-        }
-        __syncwarp();
-        if (it > 0) {
-          ok = issue_pv(it - 1);
-          if (!ok) break;
         }
       }
-      w += s.ntiles;
+      __syncwarp();
+      if (action == 1) ++pv; else ++qk;
     }
-    if (ok && it > 0) issue_pv(it - 1);
   } else {
     // ---------------------------------------------------------- softmax warps
     const int quad = warp & 3;      // TMEM lane quadrant this warp may access
@@ -631,8 +628,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
 }
 
 template <typename T, typename OutT, int NCOL>
-cudaError_t launch_typed(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                         const DecodeParams& p, int grid, cudaStream_t stream) {
+cudaError_t launch_typed(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream) {
   auto kern = decode_sm100_kernel<T, OutT, NCOL>;
   // The attribute is per device; setting it again is harmless.
   static unsigned long long configured = 0;
@@ -645,15 +641,14 @@ cudaError_t launch_typed(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const
     if (e != cudaSuccess) return e;
     __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
   }
-  kern<<<grid, kSm100Threads, kSmemBytes, stream>>>(tm_q, tm_k, tm_v, p);
+  kern<<<grid, kSm100Threads, kSmemBytes, stream>>>(m.q, m.k, m.v, m.k16, m.v16, p);
   return cudaGetLastError();
 }
 
 template <typename T, typename OutT>
-cudaError_t launch_ncol(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                        const DecodeParams& p, int grid, cudaStream_t stream) {
-  if (p.group <= 8) return launch_typed<T, OutT, 8>(tm_q, tm_k, tm_v, p, grid, stream);
-  return launch_typed<T, OutT, 16>(tm_q, tm_k, tm_v, p, grid, stream);
+cudaError_t launch_ncol(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream) {
+  if (p.group <= 8) return launch_typed<T, OutT, 8>(m, p, grid, stream);
+  return launch_typed<T, OutT, 16>(m, p, grid, stream);
 }
 
 }  // namespace
@@ -674,15 +669,14 @@ WorkspaceLayout workspace_layout(int64_t batch_per_launch, int64_t num_heads_k, 
   return w;
 }
 
-cudaError_t launch_decode_sm100(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
-                                const CUtensorMap& tm_v, const DecodeParams& p, int dtype,
+cudaError_t launch_decode_sm100(const TensorMaps& m, const DecodeParams& p, int dtype,
                                 bool out_fp32, int grid, cudaStream_t stream) {
   if (dtype == 0) {
-    return out_fp32 ? launch_ncol<__nv_bfloat16, float>(tm_q, tm_k, tm_v, p, grid, stream)
-                    : launch_ncol<__nv_bfloat16, __nv_bfloat16>(tm_q, tm_k, tm_v, p, grid, stream);
+    return out_fp32 ? launch_ncol<__nv_bfloat16, float>(m, p, grid, stream)
+                    : launch_ncol<__nv_bfloat16, __nv_bfloat16>(m, p, grid, stream);
   }
-  return out_fp32 ? launch_ncol<__half, float>(tm_q, tm_k, tm_v, p, grid, stream)
-                  : launch_ncol<__half, __half>(tm_q, tm_k, tm_v, p, grid, stream);
+  return out_fp32 ? launch_ncol<__half, float>(m, p, grid, stream)
+                  : launch_ncol<__half, __half>(m, p, grid, stream);
 }
 
 }  // namespace fd

@@ -11,7 +11,7 @@ namespace fd {
 constexpr int kHeadDim = 128;          // head dim of the tensor-core path
 constexpr int kTileTokens = 128;       // KV tokens per pipeline stage (UMMA M of Q.K^T)
 constexpr int kMaxGroup = 16;          // query heads per KV head (UMMA N, padded)
-constexpr int kMaxBatchPerLaunch = 2048;  // sequences per launch (schedule lives in smem)
+constexpr int kMaxBatchPerLaunch = 1024;  // sequences per launch (schedule lives in smem)
 constexpr int kSm100Threads = 192;     // warp0 TMA, warp1 MMA, warps2-5 softmax/epilogue
 
 // Per-launch parameters of the tensor-core kernel (tensor maps travel as
@@ -30,7 +30,6 @@ struct DecodeParams {
   int* err;                   // device error word
   unsigned long long timeout_ns;
   uint32_t epoch;             // 1 .. 2^20-1, different for consecutive launches
-  int prefetch_tiles;         // L2 prefetch distance in tiles (0 = off)
 };
 
 struct SimtParams {
@@ -50,9 +49,15 @@ struct WorkspaceLayout {
 WorkspaceLayout workspace_layout(int64_t batch_per_launch, int64_t num_heads_k, int64_t group,
                                  int grid_max);
 
+// TMA descriptors of one launch: q rows [B, Hq, 128] (box 64 x group), K and
+// V caches [num_blocks, page, Hkv, 128] with `chunk`-token boxes for full
+// tiles and 16-token boxes for a sequence's last partial tile.
+struct TensorMaps {
+  CUtensorMap q, k, v, k16, v16;
+};
+
 // Launchers.  dtype: 0 bf16, 1 fp16; out_fp32 selects an fp32 output.
-cudaError_t launch_decode_sm100(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
-                                const CUtensorMap& tm_v, const DecodeParams& p, int dtype,
+cudaError_t launch_decode_sm100(const TensorMaps& m, const DecodeParams& p, int dtype,
                                 bool out_fp32, int grid, cudaStream_t stream);
 cudaError_t launch_decode_simt(const SimtParams& p, int dtype, bool out_fp32, cudaStream_t stream);
 cudaError_t launch_combine_lse(const float* part_o, int64_t o_stride, const float* part_lse,

@@ -12,7 +12,7 @@ from __future__ import annotations
 from dataclasses import dataclass
 
 TILE_TOKENS = 128
-MAX_BATCH_PER_LAUNCH = 2048
+MAX_BATCH_PER_LAUNCH = 1024
 
 
 @dataclass(frozen=True)
