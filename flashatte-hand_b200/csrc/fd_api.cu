@@ -157,6 +157,17 @@ unsigned long long timeout_ns() {
 
 }  // namespace
 
+namespace fd {
+int report_error(int code, const char* fmt, ...) {
+  t_last_error = code;
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_msg, sizeof(t_last_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+}  // namespace fd
+
 extern "C" {
 
 const char* fd_version(void) { return "flashdecode-sm100 0.1.0"; }

@@ -69,4 +69,8 @@ cudaError_t launch_bounded_wait_probe(unsigned long long budget_ns, int* status,
 
 size_t sm100_smem_bytes();
 
+// Record `code` and a printf-style message as this thread's last error (what
+// fd_last_error / fd_last_error_message report) and return `code`.
+int report_error(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+
 }  // namespace fd

@@ -91,6 +91,31 @@ int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, voi
                     int64_t max_seqlen_k, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * fd_decode_paged_noalloc - fd_decode_paged for callers that cannot allocate
+ * device memory: a process whose framework allocator already holds nearly
+ * all of the GPU's memory (a library cudaMalloc would fail or fragment that
+ * pool), or a serving loop that allocates everything at start-up and forbids
+ * allocation afterwards.  Same arguments as fd_decode_paged without the
+ * workspace: the split scratch is a fixed 8 MiB array inside the library's
+ * device image, held on every GPU that loads the library until the process
+ * exits.  Shapes needing more scratch than that (fd_decode_workspace_size >
+ * 8 MiB) are rejected with FD_ERR_WORKSPACE.  Calls no cudaMalloc/cudaFree
+ * or other allocating routine.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress, that device current), so make
+ * that first call before any stream capture.  All calls share the array and
+ * it keeps the previous call's contents (the call clears what must start at
+ * zero): calls that can overlap on the GPU race with each other.
+ * No counterpart in the reference, whose run_kernel always cudaMallocs its
+ * split workspace on first use.
+ */
+int fd_decode_paged_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out,
+                            float* lse, const int32_t* cache_seqlens, const int32_t* block_table,
+                            int64_t block_table_stride, int64_t batch_size, int64_t num_heads,
+                            int64_t num_heads_k, int64_t headdim, int64_t page_block_size,
+                            int64_t num_blocks, int dtype, int out_dtype, float softmax_scale,
+                            int64_t max_seqlen_k, void* stream);
+
+/*
  * fd_decode_workspace_size - bytes of workspace fd_decode_paged needs for
  * these shapes on the current device.
  * Replaces: reserve_split_workspace sizing (best :1078-1133, :1343-1348),
