@@ -201,6 +201,7 @@ def main():
 
     import flashdecode
     from flashdecode import cases
+    from flashdecode import dist as fdist
 
     torch.cuda.set_device(local)
     dist = None
@@ -210,17 +211,42 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    case = cases.config_case(args.config)
-    t = cases.materialize(case, "cuda", seed=rank)
-    stream = torch.cuda.current_stream()
+    full = cases.config_case(args.config)
     lib = flashdecode.load_library()
+    stream = torch.cuda.current_stream()
+    splitter = None
+    if world == 1 or args.config in (1, 2):
+        # every rank decodes its own full batch: batch sharding of a B*N batch
+        case, scaling, parallel = full, "weak", f"dp{world}"
+        total_kv = full.kv_bytes() * world
+        t = cases.materialize(case, "cuda", seed=rank)
+    elif args.config in (3, 5):
+        # the configured batch split over the ranks, longest sequences first
+        case, _rows = fdist.batch_shard(full, rank, world)
+        scaling, parallel = "strong", f"batch-shard{world}"
+        total_kv = full.kv_bytes()
+        t = cases.materialize(case, "cuda", seed=rank)
+    else:
+        # config 4: every rank holds a page range of each sequence; partials
+        # are all-gathered over NCCL and merged
+        case, _page_map = fdist.kv_split_case(full, rank, world)
+        scaling, parallel = "strong", f"splitkv{world}"
+        total_kv = full.kv_bytes()
+        t = cases.materialize(case, "cuda", seed=0)  # same q on every rank
+        splitter = fdist.SplitKVDecode(case.B, case.Hq, case.D, case.dtype, "cuda")
+    max_len = max(int(case.seqlens.max()), 1)
+
+    def decode(q, seqlens, bt):
+        if splitter is not None:
+            return splitter(q, t["k_cache"], t["v_cache"], seqlens, bt, case.softmax_scale)
+        return flashdecode.flash_decode(q, t["k_cache"], t["v_cache"], seqlens, bt,
+                                        softmax_scale=case.softmax_scale, return_softmax_lse=True,
+                                        max_seqlen_k=max_len)
 
     def step():
-        flashdecode.flash_decode(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"],
-                                 t["block_table"], softmax_scale=case.softmax_scale,
-                                 return_softmax_lse=True, max_seqlen_k=int(case.seqlens.max()))
+        decode(t["q"], t["cache_seqlens"], t["block_table"])
 
-    launches_per_call = math.ceil(case.B / 1024)
+    launches_per_call = math.ceil(case.B / 1024) + (1 if splitter is not None else 0)
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
@@ -257,9 +283,7 @@ def main():
             dq.copy_(hq, non_blocking=True)
             ds.copy_(hs, non_blocking=True)
             db.copy_(hb, non_blocking=True)
-            o, l = flashdecode.flash_decode(dq, t["k_cache"], t["v_cache"], ds, db,
-                                            softmax_scale=case.softmax_scale, return_softmax_lse=True,
-                                            max_seqlen_k=int(case.seqlens.max()))
+            o, l = decode(dq, ds, db)
             ho.copy_(o, non_blocking=True)
             hl.copy_(l, non_blocking=True)
 
@@ -282,7 +306,7 @@ def main():
             e_ms = float(tt.item())
         h2d = hq.numel() * hq.element_size() + hs.numel() * 4 + hb.numel() * 4
         d2h = ho.numel() * ho.element_size() + hl.numel() * 4
-        e2e = {"value": round(case.kv_bytes() * world / (e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+        e2e = {"value": round(total_kv / (e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "us_per_call": round(e_ms * 1e3, 2),
                "steps": e_steps, "kv_cache": "resident in HBM (decode state, not a per-step input)"}
 
@@ -292,12 +316,13 @@ def main():
         return
 
     per_call_s = ms * 1e-3 / args.steps
-    kv_gbs = case.kv_bytes() * world / per_call_s / 1e9
+    kv_gbs = total_kv / per_call_s / 1e9
     alg_per_launch = case.algorithmic_bytes(with_lse=True)
     achieved = alg_per_launch / per_call_s / 1e9
     peak, peak_kind = peaks()
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": profile_traffic(f"cfg{args.config}"),
+                "frac": round(achieved / peak, 4),
+                "traffic": profile_traffic(f"cfg{args.config}") if world == 1 else None,
                 "peak_source": peak_kind, "kernel": "decode_sm100_kernel",
                 "alg_bytes_per_launch": alg_per_launch}
     cpu = None
@@ -311,11 +336,11 @@ def main():
         "metric": METRIC, "value": round(kv_gbs, 2), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_call_s * 1e3, 5),
         "us_per_call": round(per_call_s * 1e6, 2), "pct_of_peak": round(100 * kv_gbs / world / peak, 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
         "dtype": "bf16" if case.dtype == torch.bfloat16 else "fp16", "data": "synthetic",
-        "config": {"workload": case.name, "global_batch": case.B * world,
-                   "seq_len": int(case.seqlens.max()), "parallelism": f"dp{world}",
-                   "Hq": case.Hq, "Hkv": case.Hkv, "head_dim": case.D, "page": case.page,
+        "config": {"workload": full.name, "global_batch": full.B * (world if scaling == "weak" else 1),
+                   "seq_len": int(full.seqlens.max()), "parallelism": parallel,
+                   "Hq": full.Hq, "Hkv": full.Hkv, "head_dim": full.D, "page": full.page,
                    "l2": "inputs larger than L2 (KV cache > 126 MB), no flush"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": launches_per_call * args.steps, "clocks": clk.summary(),

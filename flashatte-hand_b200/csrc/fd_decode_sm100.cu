@@ -56,8 +56,8 @@ constexpr int kOffP = kOffStages + kStages * kStageBytes;
 constexpr int kOffBars = kOffP + 2 * kPBufBytes;
 constexpr int kOffMisc = kOffBars + kNumBars * 8;            // tmem slot, abort, last flag
 constexpr int kOffRed = (kOffMisc + 64 + 15) & ~15;          // [2][4][16] floats tile maxima
-constexpr int kOffFin = kOffRed + 2 * 4 * kMaxGroup * 4;     // [4][16] floats row sums
-constexpr int kOffPrefix = kOffFin + 4 * kMaxGroup * 4;      // [B+1] ints tile prefix sums
+constexpr int kOffFin = kOffRed + 2 * 4 * kMaxGroup * 4;     // [2][4][16] floats row sums
+constexpr int kOffPrefix = kOffFin + 2 * 4 * kMaxGroup * 4;  // [B+1] ints tile prefix sums
 constexpr int kSmemUsed = kOffPrefix + (kMaxBatchPerLaunch + 1) * 4;
 constexpr int kSmemBytes = kSmemUsed + 1024;                 // slack for 1024-B alignment
 static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
@@ -434,176 +434,222 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     }
   } else {
     // ---------------------------------------------------------- softmax warps
-    const int quad = warp & 3;      // TMEM lane quadrant this warp may access
+    // One flat loop over the CTA's tiles.  Iteration i runs the softmax of
+    // tile i, then folds in O of tile i-1.  When tile i opens a new segment,
+    // O of the previous segment's last tile arrives in that same iteration
+    // and the previous segment is finished there, so the P.V round trip of a
+    // segment's last tile overlaps the next segment's first softmax.
+    const int quad = warp & 3;         // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;  // token row of S, head-dim index of O
+    const int d = row;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     const float neg_inf = -__int_as_float(0x7f800000);
     const int hq = p.num_heads;
     OutT* out = reinterpret_cast<OutT*>(p.out);
-    int64_t it = 0;
-    for (int64_t w = w_begin; w < w_end;) {
-      const Segment s = locate(prefix, batch, hkv, total, grid, w, w_end, p.seqlens, max_len);
-      float m_run[NCOL], l_run[NCOL], o_acc[NCOL], a_prev[NCOL];
+    const int64_t ntiles = w_end - w_begin;
+
+    struct State {
+      float m[NCOL], l[NCOL], o[NCOL], a[NCOL];
+    };
+    auto reset = [&](State& st) {
 #pragma unroll
       for (int h = 0; h < NCOL; ++h) {
-        m_run[h] = neg_inf;
-        l_run[h] = 0.f;
-        o_acc[h] = 0.f;
-        a_prev[h] = 0.f;
+        st.m[h] = neg_inf;
+        st.l[h] = 0.f;
+        st.o[h] = 0.f;
+        st.a[h] = 0.f;
       }
-      auto consume_o = [&](int64_t i) {
-        const int pb = static_cast<int>(i & 1);
-        mbar_wait_bounded(&o_full[pb], static_cast<uint32_t>((i >> 1) & 1), abort_flag, budget);
-        tc_fence_after();
-        uint32_t r[kPvN];
-        if constexpr (NCOL == 8) tmem_ld_x16(lane_addr + col_o(pb), r); else tmem_ld_x32(lane_addr + col_o(pb), r);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&o_empty[pb]);
+    };
+    // O^T of tile i (hi + lo halves) for this thread's head-dim row.
+    auto load_o = [&](int64_t i, float (&ov)[NCOL]) {
+      const int pb = static_cast<int>(i & 1);
+      mbar_wait_bounded(&o_full[pb], static_cast<uint32_t>((i >> 1) & 1), abort_flag, budget);
+      tc_fence_after();
+      uint32_t r[kPvN];
+      if constexpr (NCOL == 8) tmem_ld_x16(lane_addr + col_o(pb), r); else tmem_ld_x32(lane_addr + col_o(pb), r);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&o_empty[pb]);
 #pragma unroll
-        for (int h = 0; h < NCOL; ++h)
-          o_acc[h] = fmaf(o_acc[h], a_prev[h], __uint_as_float(r[h]) + __uint_as_float(r[NCOL + h]));
-      };
-      for (int t = 0; t < s.ntiles; ++t, ++it) {
-        const int sb = static_cast<int>(it & 1);
-        const int stage = static_cast<int>(it % kStages);
-        mbar_wait_bounded(&s_full[sb], static_cast<uint32_t>((it >> 1) & 1), abort_flag, budget);
-        tc_fence_after();
-        uint32_t r[NCOL];
-        if constexpr (NCOL == 8) tmem_ld_x8(lane_addr + col_s(sb), r); else tmem_ld_x16(lane_addr + col_s(sb), r);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&s_empty[sb]);
-
-        const int tok0 = (s.tile0 + t) * kTileTokens;
-        const int valid_rows = s.seqlen - tok0;  // may exceed 128; <=0 only for empty sequences
-        const bool valid = row < valid_rows;
-        float sv[NCOL];
-        float* red_t = red + (it & 1) * (4 * kMaxGroup);
-#pragma unroll
-        for (int h = 0; h < NCOL; ++h) {
-          sv[h] = valid ? __uint_as_float(r[h]) * p.scale_log2 : neg_inf;
-          const float wm = warp_max_f32(sv[h]);
-          if (lane == 0) red_t[quad * kMaxGroup + h] = wm;
-        }
-        named_bar_sync(1, 128);
-        float pv[NCOL];
-#pragma unroll
-        for (int h = 0; h < NCOL; ++h) {
-          const float tmax = fmaxf(fmaxf(red_t[h], red_t[kMaxGroup + h]),
-                                   fmaxf(red_t[2 * kMaxGroup + h], red_t[3 * kMaxGroup + h]));
-          const float m_new = fmaxf(m_run[h], tmax);
-          const float m_use = m_new == neg_inf ? 0.f : m_new;
-          const float alpha = fast_exp2(m_run[h] - m_use);
-          const float pe = (h < group) ? fast_exp2(sv[h] - m_use) : 0.f;
-          l_run[h] = fmaf(l_run[h], alpha, pe);
-          m_run[h] = m_new;
-          pv[h] = pe;
-          sv[h] = alpha;  // keep this tile's rescale factor
-        }
-        if (valid_rows < kTileTokens && !valid) {
-          // Rows past the sequence end: stale or never-written data must not
-          // reach P.V (0 * NaN), so zero this token's V row in the stage.
-          uint4* vrow0 = reinterpret_cast<uint4*>(stages + stage * kStageBytes + kOperandBytes + row * 128);
-          uint4* vrow1 = reinterpret_cast<uint4*>(stages + stage * kStageBytes + kOperandBytes + kHalfBytes + row * 128);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            vrow0[i] = make_uint4(0, 0, 0, 0);
-            vrow1[i] = make_uint4(0, 0, 0, 0);
-          }
-        }
-        {
-          // This token's row of [P_hi | P_lo]: 8-column chunks 128 B apart.
-          uint8_t* prow = pbufs + sb * kPBufBytes + (row >> 3) * kPGroupBytes + (row & 7) * 16;
-#pragma unroll
-          for (int c = 0; c < NCOL / 8; ++c) {
-            uint4 hi, lo;
-            DType<T>::split2(pv[8 * c + 0], pv[8 * c + 1], hi.x, lo.x);
-            DType<T>::split2(pv[8 * c + 2], pv[8 * c + 3], hi.y, lo.y);
-            DType<T>::split2(pv[8 * c + 4], pv[8 * c + 5], hi.z, lo.z);
-            DType<T>::split2(pv[8 * c + 6], pv[8 * c + 7], hi.w, lo.w);
-            *reinterpret_cast<uint4*>(prow + c * 128) = hi;
-            *reinterpret_cast<uint4*>(prow + (NCOL / 8 + c) * 128) = lo;
-          }
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(&p_full[sb]);
-        if (t > 0) consume_o(it - 1);
-#pragma unroll
-        for (int h = 0; h < NCOL; ++h) a_prev[h] = sv[h];
-      }
-      consume_o(it - 1);
-
-      // ---- segment epilogue: row sums across the 128 threads
+      for (int h = 0; h < NCOL; ++h) ov[h] = __uint_as_float(r[h]) + __uint_as_float(r[NCOL + h]);
+    };
+    // Segment epilogue: direct output, or partial + (last arrival) merge.
+    int fin_buf = 0;
+    auto finish = [&](const Segment& sg, const State& st) {
+      float* fb = fin + fin_buf * (4 * kMaxGroup);
+      fin_buf ^= 1;
 #pragma unroll
       for (int h = 0; h < NCOL; ++h) {
-        float v = l_run[h];
+        float v = st.l[h];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0) fin[quad * kMaxGroup + h] = v;
+        if (lane == 0) fb[quad * kMaxGroup + h] = v;
       }
       named_bar_sync(1, 128);
       float l_tot[NCOL];
 #pragma unroll
       for (int h = 0; h < NCOL; ++h)
-        l_tot[h] = (fin[h] + fin[kMaxGroup + h]) + (fin[2 * kMaxGroup + h] + fin[3 * kMaxGroup + h]);
-      const int d = row;
-      if (s.nseg == 1) {
-        const int64_t obase = (static_cast<int64_t>(s.b) * hq + s.kvh * group) * kHeadDim + d;
+        l_tot[h] = (fb[h] + fb[kMaxGroup + h]) + (fb[2 * kMaxGroup + h] + fb[3 * kMaxGroup + h]);
+      if (sg.nseg == 1) {
+        const int64_t obase = (static_cast<int64_t>(sg.b) * hq + sg.kvh * group) * kHeadDim + d;
 #pragma unroll
         for (int h = 0; h < NCOL; ++h) {
           if (h < group) {
-            const float v = l_tot[h] > 0.f ? o_acc[h] / l_tot[h] : 0.f;
+            const float v = l_tot[h] > 0.f ? st.o[h] / l_tot[h] : 0.f;
             out[obase + static_cast<int64_t>(h) * kHeadDim] = to_out<OutT>(v);
             if (p.lse != nullptr && d == h) {
-              p.lse[static_cast<int64_t>(s.b) * hq + s.kvh * group + h] =
-                  l_tot[h] > 0.f ? (m_run[h] + fast_log2(l_tot[h])) * 0.69314718055994531f : neg_inf;
+              p.lse[static_cast<int64_t>(sg.b) * hq + sg.kvh * group + h] =
+                  l_tot[h] > 0.f ? (st.m[h] + fast_log2(l_tot[h])) * 0.69314718055994531f : neg_inf;
             }
           }
         }
-      } else {
-        const int64_t slot = static_cast<int64_t>(cta) + s.pair;
-        float* po = p.part_o + slot * group * kHeadDim + d;
+        return;
+      }
+      const int64_t slot = static_cast<int64_t>(cta) + sg.pair;
+      float* po = p.part_o + slot * group * kHeadDim + d;
 #pragma unroll
-        for (int h = 0; h < NCOL; ++h) {
-          if (h < group) {
-            po[h * kHeadDim] = l_tot[h] > 0.f ? o_acc[h] / l_tot[h] : 0.f;
-            if (d == h) p.part_lse[slot * group + h] = l_tot[h] > 0.f ? m_run[h] + fast_log2(l_tot[h]) : neg_inf;
-          }
-        }
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (d == 0) {
-          int is_last = 0;
-          if (!*abort_flag) is_last = ticket_arrive(p.tickets + s.pair, p.epoch, s.nseg) ? 1 : 0;
-          *last_flag = is_last;
-        }
-        named_bar_sync(1, 128);
-        if (*last_flag) {
-          __threadfence();
-          const int64_t sbase = static_cast<int64_t>(s.cfirst) + s.pair;
-          for (int h = 0; h < group; ++h) {
-            float mx = neg_inf;
-            for (int j = 0; j < s.nseg; ++j) mx = fmaxf(mx, __ldcg(p.part_lse + (sbase + j) * group + h));
-            float den = 0.f, acc = 0.f;
-            for (int j = 0; j < s.nseg; ++j) {
-              const float lj = __ldcg(p.part_lse + (sbase + j) * group + h);
-              const float wj = lj == neg_inf ? 0.f : fast_exp2(lj - mx);
-              if (wj > 0.f) {
-                acc = fmaf(wj, __ldcg(p.part_o + ((sbase + j) * group + h) * kHeadDim + d), acc);
-                den += wj;
-              }
-            }
-            const int64_t oidx = (static_cast<int64_t>(s.b) * hq + s.kvh * group + h) * kHeadDim + d;
-            out[oidx] = to_out<OutT>(den > 0.f ? acc / den : 0.f);
-            if (p.lse != nullptr && d == 0)
-              p.lse[static_cast<int64_t>(s.b) * hq + s.kvh * group + h] =
-                  den > 0.f ? (mx + fast_log2(den)) * 0.69314718055994531f : neg_inf;
-          }
+      for (int h = 0; h < NCOL; ++h) {
+        if (h < group) {
+          po[h * kHeadDim] = l_tot[h] > 0.f ? st.o[h] / l_tot[h] : 0.f;
+          if (d == h) p.part_lse[slot * group + h] = l_tot[h] > 0.f ? st.m[h] + fast_log2(l_tot[h]) : neg_inf;
         }
       }
-      named_bar_sync(1, 128);  // fin / last_flag are reused by the next segment
-      w += s.ntiles;
+      __threadfence();
+      named_bar_sync(1, 128);
+      if (d == 0) {
+        int is_last = 0;
+        if (!*abort_flag) is_last = ticket_arrive(p.tickets + sg.pair, p.epoch, sg.nseg) ? 1 : 0;
+        *last_flag = is_last;
+      }
+      named_bar_sync(1, 128);
+      const int merge = *last_flag;
+      named_bar_sync(1, 128);  // last_flag is reused by the next split segment
+      if (!merge) return;
+      __threadfence();
+      const int64_t sbase = static_cast<int64_t>(sg.cfirst) + sg.pair;
+      for (int h = 0; h < group; ++h) {
+        float mx = neg_inf;
+        for (int j = 0; j < sg.nseg; ++j) mx = fmaxf(mx, __ldcg(p.part_lse + (sbase + j) * group + h));
+        float den = 0.f, acc = 0.f;
+        for (int j = 0; j < sg.nseg; ++j) {
+          const float lj = __ldcg(p.part_lse + (sbase + j) * group + h);
+          const float wj = lj == neg_inf ? 0.f : fast_exp2(lj - mx);
+          if (wj > 0.f) {
+            acc = fmaf(wj, __ldcg(p.part_o + ((sbase + j) * group + h) * kHeadDim + d), acc);
+            den += wj;
+          }
+        }
+        const int64_t oidx = (static_cast<int64_t>(sg.b) * hq + sg.kvh * group + h) * kHeadDim + d;
+        out[oidx] = to_out<OutT>(den > 0.f ? acc / den : 0.f);
+        if (p.lse != nullptr && d == 0)
+          p.lse[static_cast<int64_t>(sg.b) * hq + sg.kvh * group + h] =
+              den > 0.f ? (mx + fast_log2(den)) * 0.69314718055994531f : neg_inf;
+      }
+    };
+
+    State cur, prev;
+    reset(cur);
+    reset(prev);
+    Segment seg{}, prev_seg{};
+    int64_t w = w_begin;
+    int t = 0;
+    if (ntiles > 0) seg = locate(prefix, batch, hkv, total, grid, w, w_end, p.seqlens, max_len);
+    for (int64_t it = 0; it < ntiles; ++it, ++t) {
+      bool prev_open = false;
+      if (t == seg.ntiles) {  // next segment
+        w += seg.ntiles;
+        prev_seg = seg;
+        seg = locate(prefix, batch, hkv, total, grid, w, w_end, p.seqlens, max_len);
+        t = 0;
+        prev = cur;
+        reset(cur);
+        prev_open = true;
+      }
+      // ---- softmax of tile `it`
+      const int sb = static_cast<int>(it & 1);
+      const int stage = static_cast<int>(it % kStages);
+      mbar_wait_bounded(&s_full[sb], static_cast<uint32_t>((it >> 1) & 1), abort_flag, budget);
+      tc_fence_after();
+      uint32_t r[NCOL];
+      if constexpr (NCOL == 8) tmem_ld_x8(lane_addr + col_s(sb), r); else tmem_ld_x16(lane_addr + col_s(sb), r);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);
+
+      const int tok0 = (seg.tile0 + t) * kTileTokens;
+      const int valid_rows = seg.seqlen - tok0;  // may exceed 128; <=0 only for empty sequences
+      const bool valid = row < valid_rows;
+      float sv[NCOL];
+      float* red_t = red + (it & 1) * (4 * kMaxGroup);
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) {
+        sv[h] = valid ? __uint_as_float(r[h]) * p.scale_log2 : neg_inf;
+        const float wm = warp_max_f32(sv[h]);
+        if (lane == 0) red_t[quad * kMaxGroup + h] = wm;
+      }
+      named_bar_sync(1, 128);
+      float pv[NCOL], alpha[NCOL];
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) {
+        const float tmax = fmaxf(fmaxf(red_t[h], red_t[kMaxGroup + h]),
+                                 fmaxf(red_t[2 * kMaxGroup + h], red_t[3 * kMaxGroup + h]));
+        const float m_new = fmaxf(cur.m[h], tmax);
+        const float m_use = m_new == neg_inf ? 0.f : m_new;
+        alpha[h] = fast_exp2(cur.m[h] - m_use);
+        pv[h] = (h < group) ? fast_exp2(sv[h] - m_use) : 0.f;
+        cur.l[h] = fmaf(cur.l[h], alpha[h], pv[h]);
+        cur.m[h] = m_new;
+      }
+      if (valid_rows < kTileTokens && !valid) {
+        // Rows past the sequence end: stale or never-written data must not
+        // reach P.V (0 * NaN), so zero this token's V row in the stage.
+        uint4* vrow0 = reinterpret_cast<uint4*>(stages + stage * kStageBytes + kOperandBytes + row * 128);
+        uint4* vrow1 = reinterpret_cast<uint4*>(stages + stage * kStageBytes + kOperandBytes + kHalfBytes + row * 128);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          vrow0[i] = make_uint4(0, 0, 0, 0);
+          vrow1[i] = make_uint4(0, 0, 0, 0);
+        }
+      }
+      {
+        // This token's row of [P_hi | P_lo]: 8-column chunks 128 B apart.
+        uint8_t* prow = pbufs + sb * kPBufBytes + (row >> 3) * kPGroupBytes + (row & 7) * 16;
+#pragma unroll
+        for (int c = 0; c < NCOL / 8; ++c) {
+          uint4 hi, lo;
+          DType<T>::split2(pv[8 * c + 0], pv[8 * c + 1], hi.x, lo.x);
+          DType<T>::split2(pv[8 * c + 2], pv[8 * c + 3], hi.y, lo.y);
+          DType<T>::split2(pv[8 * c + 4], pv[8 * c + 5], hi.z, lo.z);
+          DType<T>::split2(pv[8 * c + 6], pv[8 * c + 7], hi.w, lo.w);
+          *reinterpret_cast<uint4*>(prow + c * 128) = hi;
+          *reinterpret_cast<uint4*>(prow + (NCOL / 8 + c) * 128) = lo;
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&p_full[sb]);
+
+      // ---- O of tile it-1
+      if (it > 0) {
+        float ov[NCOL];
+        load_o(it - 1, ov);
+        if (prev_open) {
+#pragma unroll
+          for (int h = 0; h < NCOL; ++h) prev.o[h] = fmaf(prev.o[h], prev.a[h], ov[h]);
+          finish(prev_seg, prev);
+        } else {
+#pragma unroll
+          for (int h = 0; h < NCOL; ++h) cur.o[h] = fmaf(cur.o[h], cur.a[h], ov[h]);
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) cur.a[h] = alpha[h];
+    }
+    if (ntiles > 0) {
+      float ov[NCOL];
+      load_o(ntiles - 1, ov);
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) cur.o[h] = fmaf(cur.o[h], cur.a[h], ov[h]);
+      finish(seg, cur);
     }
   }
 

@@ -1,0 +1,106 @@
+"""Multi-GPU decode on one node (NCCL, 2 ranks, one process per GPU): the
+cross-GPU split-KV exchange and batch sharding against the single-GPU result.
+Skipped when fewer than two GPUs are visible."""
+import datetime
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, port, kind, q):
+    try:
+        import sys
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        for p in (root, os.path.join(root, "flashatte-hand_b200")):
+            if p not in sys.path:
+                sys.path.insert(0, p)
+        import torch.distributed as dist
+
+        import flashdecode
+        from flashdecode import cases, dist as fdist
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=WORLD,
+                                timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        glob = cases.custom_case("mg", torch.bfloat16, [20000, 3, 7777, 0, 40000], 32, 8,
+                                 page=256, seed=5)
+        t = cases.materialize(glob, "cuda", seed=5)  # identical on every rank
+        ref_o, ref_l = flashdecode.flash_decode(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"],
+                                                t["block_table"], return_softmax_lse=True)
+        if kind == "splitkv":
+            local, page_map = fdist.kv_split_case(glob, rank, WORLD)
+            pm = page_map.to("cuda")
+            k, v = t["k_cache"][pm].contiguous(), t["v_cache"][pm].contiguous()
+            step = fdist.SplitKVDecode(glob.B, glob.Hq, glob.D, torch.bfloat16, "cuda")
+            for _ in range(2):
+                out, lse = step(t["q"], k, v, local.seqlens.cuda(), local.block_table.cuda(),
+                                glob.softmax_scale)
+            torch.cuda.synchronize()
+            err = (out.float() - ref_o.float()).abs()
+            assert bool((err <= 2e-3 + 1e-2 * ref_o.float().abs()).all()), float(err.max())
+            fin = torch.isfinite(ref_l)
+            assert torch.equal(fin, torch.isfinite(lse))
+            assert torch.allclose(lse[fin], ref_l[fin], atol=1e-3)
+        else:
+            sub, rows = fdist.batch_shard(glob, rank, WORLD)
+            used = glob.block_table[rows][glob.block_table[rows] >= 0].unique(sorted=True).long().cuda()
+            k, v = t["k_cache"][used].contiguous(), t["v_cache"][used].contiguous()
+            out, lse = flashdecode.flash_decode(t["q"][rows].contiguous(), k, v, sub.seqlens.cuda(),
+                                                sub.block_table.cuda(), return_softmax_lse=True)
+            torch.cuda.synchronize()
+            # a different batch splits differently across CTAs: compare within tolerance
+            err = (out.float() - ref_o[rows].float()).abs()
+            assert bool((err <= 2e-3 + 1e-2 * ref_o[rows].float().abs()).all()), float(err.max())
+            fin = torch.isfinite(ref_l[rows])
+            assert torch.equal(fin, torch.isfinite(lse))
+            assert torch.allclose(lse[fin], ref_l[rows][fin], atol=1e-3)
+            got = [None] * WORLD
+            dist.all_gather_object(got, rows)
+            assert sorted(sum(got, [])) == list(range(glob.B))
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put(("ok", rank))
+    except Exception:
+        q.put(("error", traceback.format_exc()))
+
+
+def _run(kind):
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, port, kind, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=240) for _ in range(WORLD)]
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert all(r[0] == "ok" for r in res), res
+
+
+def test_split_kv_across_two_gpus():
+    _run("splitkv")
+
+
+def test_batch_shard_across_two_gpus():
+    _run("batch")
