@@ -246,7 +246,7 @@ def main():
     def step():
         decode(t["q"], t["cache_seqlens"], t["block_table"])
 
-    launches_per_call = math.ceil(case.B / 1024) + (1 if splitter is not None else 0)
+    launches_per_call = math.ceil(case.B / 512) + (1 if splitter is not None else 0)
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()

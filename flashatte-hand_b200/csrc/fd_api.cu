@@ -26,6 +26,8 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 constexpr unsigned long long kDefaultTimeoutNs = 1000000000ull;  // 1 s per in-kernel wait
+constexpr int kDefaultCostTile = 2;
+constexpr int kDefaultCostSeg = 12;
 
 thread_local int t_last_error = FD_OK;
 thread_local char t_last_msg[256] = "ok";
@@ -141,6 +143,23 @@ CUresult encode(CUtensorMap* m, int dtype, int rank, const void* base, const cuu
 uint32_t next_epoch() {
   static std::atomic<uint32_t> counter{0};
   return counter.fetch_add(1, std::memory_order_relaxed) % 0xFFFFFu + 1u;
+}
+
+// Split cost model (units: a full tile's K/V bytes = 8): fixed cost per
+// tile and per (sequence, KV head) pair.  FD_COST_TILE / FD_COST_SEG override.
+int env_int(const char* name, int dflt, int lo, int hi) {
+  const char* e = std::getenv(name);
+  if (e == nullptr) return dflt;
+  const long x = std::strtol(e, nullptr, 10);
+  return (x >= lo && x <= hi) ? static_cast<int>(x) : dflt;
+}
+int cost_tile() {
+  static const int v = env_int("FD_COST_TILE", kDefaultCostTile, 0, 64);
+  return v;
+}
+int cost_seg() {
+  static const int v = env_int("FD_COST_SEG", kDefaultCostSeg, 1, 256);
+  return v;
 }
 
 unsigned long long timeout_ns() {
@@ -299,9 +318,16 @@ int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, voi
     if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "K/V tensor map encode failed (%d)", (int)r);
   }
 
-  for (int64_t b0 = 0; b0 < batch_size; b0 += fd::kMaxBatchPerLaunch) {
-    const int64_t nb = batch_size - b0 < fd::kMaxBatchPerLaunch ? batch_size - b0
-                                                                 : fd::kMaxBatchPerLaunch;
+  // The kernel keeps per-sequence cost prefix sums in int32: bound the batch
+  // of one launch so the sum cannot overflow.
+  const int64_t per_seq_cost =
+      cost_seg() + ((kv_max + fd::kTileTokens - 1) / fd::kTileTokens + 1) *
+                       (8 + static_cast<int64_t>(cost_tile()));
+  if (per_seq_cost > INT32_MAX) return set_error(FD_ERR_UNSUPPORTED, "sequence too long");
+  int64_t per_launch = INT32_MAX / per_seq_cost;
+  if (per_launch > fd::kMaxBatchPerLaunch) per_launch = fd::kMaxBatchPerLaunch;
+  for (int64_t b0 = 0; b0 < batch_size; b0 += per_launch) {
+    const int64_t nb = batch_size - b0 < per_launch ? batch_size - b0 : per_launch;
     {
       const uint8_t* qb = static_cast<const uint8_t*>(q) + b0 * num_heads * 128 * es;
       const cuuint64_t dims[3] = {128, (cuuint64_t)num_heads, (cuuint64_t)nb};
@@ -329,6 +355,8 @@ int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, voi
     p.part_o = reinterpret_cast<float*>(ws + wl.o_off);
     p.timeout_ns = timeout_ns();
     p.epoch = next_epoch();
+    p.cost_tile = cost_tile();
+    p.cost_seg = cost_seg();
     const int64_t work_bound = nb * num_heads_k * tiles_bound;
     const int grid = static_cast<int>(work_bound < sms ? work_bound : sms);
     const cudaError_t e = fd::launch_decode_sm100(maps, p, dtype, out_fp32, grid, st);

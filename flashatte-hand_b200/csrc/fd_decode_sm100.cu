@@ -4,13 +4,14 @@
 // per-split grid, submission-oj/best_flashattn_kvcache_decode.cu:1039-1076,
 // :1381-1418, and its balanced page ranges :664-671): every (sequence b,
 // KV head) pair is a row of 128-token tiles; the rows are laid end to end
-// (b-major, then KV head) and the resulting line of W tiles is cut into
-// gridDim.x equal contiguous ranges, one per persistent CTA.  A CTA walks
-// its range segment by segment (a segment = the part of one pair inside the
-// range).  A pair that lies inside one CTA is written straight to the
-// output; a pair cut by range boundaries leaves one normalised partial
-// (O, log2-LSE) per segment and the CTA that finishes last merges them
-// (replaces the separate combine launch, best :956-1037, :1420-1425).
+// (b-major, then KV head) and the line is cut into contiguous ranges of
+// equal estimated cost (K/V bytes of each tile + a fixed cost per tile + a
+// fixed cost per pair), one per persistent CTA.  A CTA walks its range
+// segment by segment (a segment = the part of one pair inside the range).
+// A pair that lies inside one CTA is written straight to the output; a pair
+// cut by range boundaries leaves one normalised partial (O, log2-LSE) per
+// segment and the CTA that finishes last merges them (replaces the separate
+// combine launch, best :956-1037, :1420-1425).
 //
 // Per tile the CTA runs, warp-specialised:
 //   warp 0    TMA producer: gathers the tile's K and V rows page by page
@@ -57,8 +58,9 @@ constexpr int kOffBars = kOffP + 2 * kPBufBytes;
 constexpr int kOffMisc = kOffBars + kNumBars * 8;            // tmem slot, abort, last flag
 constexpr int kOffRed = (kOffMisc + 64 + 15) & ~15;          // [2][4][16] floats tile maxima
 constexpr int kOffFin = kOffRed + 2 * 4 * kMaxGroup * 4;     // [2][4][16] floats row sums
-constexpr int kOffPrefix = kOffFin + 2 * 4 * kMaxGroup * 4;  // [B+1] ints tile prefix sums
-constexpr int kSmemUsed = kOffPrefix + (kMaxBatchPerLaunch + 1) * 4;
+constexpr int kOffPrefix = kOffFin + 2 * 4 * kMaxGroup * 4;  // [B+1] ints pair-cost prefix sums
+constexpr int kOffLens = kOffPrefix + (kMaxBatchPerLaunch + 1) * 4;  // [B] ints clamped lengths
+constexpr int kSmemUsed = kOffLens + kMaxBatchPerLaunch * 4;
 constexpr int kSmemBytes = kSmemUsed + 1024;                 // slack for 1024-B alignment
 static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
 
@@ -136,8 +138,34 @@ template <> __device__ __forceinline__ __nv_bfloat16 to_out<__nv_bfloat16>(float
 }
 template <> __device__ __forceinline__ __half to_out<__half>(float x) { return __float2half_rn(x); }
 
-// One segment of a CTA's tile range: the tiles of pair (b, kvh) that fall in
-// [w, min(range_end, pair_end)).
+// ---------------------------------------------------------------- schedule
+// Work is split in cost space.  In units where the K/V bytes of a full
+// 128-token tile cost kFullTile = 8, a tile also costs `tile_fixed` (its
+// fixed QK / softmax / PV work), a sequence's partial last tile costs its
+// 16-token boxes instead of 8, and every (sequence, KV head) pair costs
+// `seg` once (its set-up and epilogue).  Pairs are laid end to end
+// (b-major, then KV head); CTA c takes the tiles whose start cost lies in
+// [C*c/G, C*(c+1)/G).  Every tile belongs to exactly one CTA; a pair
+// spread over several CTAs is merged by the last of them.
+constexpr int kFullTile = 8;
+
+struct CostModel {
+  int tile_fixed, seg;
+  __device__ __forceinline__ int full() const { return kFullTile + tile_fixed; }
+  // cost of one pair of a sequence of `len` tokens
+  __device__ __forceinline__ int pair_cost(int len) const {
+    const int n_full = len / kTileTokens, rem = len % kTileTokens;
+    return seg + n_full * full() + ((rem > 0 || len == 0) ? (rem + 15) / 16 + tile_fixed : 0);
+  }
+};
+
+__device__ __forceinline__ int seq_tiles(int len) {
+  return len > 0 ? (len + kTileTokens - 1) / kTileTokens : 1;
+}
+
+__device__ __forceinline__ int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// One segment of a CTA's work: tiles tile0 .. tile0+ntiles-1 of pair (b, kvh).
 struct Segment {
   int b, kvh, pair;
   int tile0, ntiles;
@@ -145,39 +173,88 @@ struct Segment {
   int nseg, cfirst;  // how many CTAs share this pair, and the first of them
 };
 
-__device__ __forceinline__ int64_t cta_of(int64_t w, int64_t total, int grid) {
-  // largest c with floor(total * c / grid) <= w
-  return ((w + 1) * grid + total - 1) / total - 1;
-}
+struct Schedule {
+  const int* cost_prefix;  // [B+1] per-pair cost prefix over sequences (smem)
+  const int* lens;         // [B] sequence lengths, clamped to [0, max_len] (smem)
+  int64_t max_len, total;  // total = Hkv * cost_prefix[B]
+  int batch, hkv, grid;
+  CostModel cm;
 
-__device__ __forceinline__ Segment locate(const int* __restrict__ prefix, int batch, int hkv,
-                                          int64_t total, int grid, int64_t w, int64_t range_end,
-                                          const int32_t* __restrict__ seqlens, int64_t max_len) {
-  int lo = 0, hi = batch - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (static_cast<int64_t>(hkv) * prefix[mid] <= w) lo = mid; else hi = mid - 1;
+  __device__ __forceinline__ int len_of(int b) const { return lens[b]; }
+  __device__ __forceinline__ int64_t range_start(int c) const { return total * c / grid; }
+  // CTA whose range holds cost position s: largest c with range_start(c) <= s
+  __device__ __forceinline__ int cta_of(int64_t s) const {
+    return static_cast<int>(((s + 1) * grid + total - 1) / total - 1);
   }
-  Segment s;
-  s.b = lo;
-  const int n = prefix[lo + 1] - prefix[lo];
-  const int64_t r = w - static_cast<int64_t>(hkv) * prefix[lo];
-  s.kvh = static_cast<int>(r / n);
-  s.tile0 = static_cast<int>(r - static_cast<int64_t>(s.kvh) * n);
-  s.pair = lo * hkv + s.kvh;
-  const int64_t pair_start = w - s.tile0;
-  const int64_t pair_end = pair_start + n;
-  const int64_t seg_end = range_end < pair_end ? range_end : pair_end;
-  s.ntiles = static_cast<int>(seg_end - w);
-  int len = __ldg(seqlens + lo);
-  len = len < 0 ? 0 : len;
-  s.seqlen = static_cast<int>(len > max_len ? max_len : len);
-  const int64_t c0 = cta_of(pair_start, total, grid);
-  const int64_t c1 = cta_of(pair_end - 1, total, grid);
-  s.cfirst = static_cast<int>(c0);
-  s.nseg = static_cast<int>(c1 - c0 + 1);
-  return s;
-}
+  __device__ __forceinline__ int64_t pair_start(int pair) const {
+    const int b = pair / hkv, kvh = pair - b * hkv;
+    return static_cast<int64_t>(hkv) * cost_prefix[b] +
+           static_cast<int64_t>(kvh) * (cost_prefix[b + 1] - cost_prefix[b]);
+  }
+  __device__ __forceinline__ int64_t tile_start(int64_t cp, int j) const {
+    return j == 0 ? cp : cp + cm.seg + static_cast<int64_t>(j) * cm.full();
+  }
+  // Segment of `pair` from tile j0 on, cut at range end e1; false if no tile
+  // of the pair at or after j0 starts before e1.  Integer work here is 32-bit
+  // except for pairs split across CTAs (rare), where cta_of is evaluated.
+  __device__ __forceinline__ bool make(int pair, int j0, int64_t e1, Segment& s) const {
+    const int b = pair / hkv;
+    const int len = len_of(b);
+    const int n = seq_tiles(len);
+    const int64_t cp = pair_start(pair);
+    if (j0 >= n || tile_start(cp, j0) >= e1) return false;
+    // last tile with start < e1: j <= ceil((e1 - cp - seg) / full) - 1
+    const int64_t x64 = e1 - cp - cm.seg;
+    int jmax = 0;
+    if (x64 > 0) {
+      const int x = x64 < 0x7fffffff ? static_cast<int>(x64) : 0x7fffffff;
+      jmax = (x + cm.full() - 1) / cm.full() - 1;
+    }
+    if (jmax > n - 1) jmax = n - 1;
+    s.b = b;
+    s.kvh = pair - b * hkv;
+    s.pair = pair;
+    s.tile0 = j0;
+    s.ntiles = jmax - j0 + 1;
+    s.seqlen = len;
+    if (j0 == 0 && jmax == n - 1) {  // the whole pair lies in this range
+      s.nseg = 1;
+      s.cfirst = -1;
+    } else {
+      s.cfirst = cta_of(cp);
+      s.nseg = cta_of(tile_start(cp, n - 1)) - s.cfirst + 1;
+    }
+    return true;
+  }
+  // First segment of CTA c (false if the CTA has no tile).
+  __device__ __forceinline__ bool first(int c, Segment& s) const {
+    if (c >= grid) return false;
+    const int64_t e0 = range_start(c), e1 = range_start(c + 1);
+    int lo = 0, hi = batch - 1;  // largest b with hkv * prefix[b] <= e0
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (static_cast<int64_t>(hkv) * cost_prefix[mid] <= e0) lo = mid; else hi = mid - 1;
+    }
+    const int pc = cost_prefix[lo + 1] - cost_prefix[lo];
+    int kvh = static_cast<int>((e0 - static_cast<int64_t>(hkv) * cost_prefix[lo]) / pc);
+    kvh = kvh < hkv - 1 ? kvh : hkv - 1;
+    const int pair = lo * hkv + kvh;
+    const int64_t cp = pair_start(pair);
+    int j0 = 0;
+    if (e0 > cp) {
+      const int64_t x = e0 - cp - cm.seg;
+      j0 = static_cast<int>(x > 0 ? ceil_div64(x, cm.full()) : 1);
+      if (j0 < 1) j0 = 1;
+    }
+    if (make(pair, j0, e1, s)) return true;
+    return pair + 1 < batch * hkv && make(pair + 1, 0, e1, s);
+  }
+  // Segment after `s` within the range that ends at cost e1.
+  __device__ __forceinline__ bool next(const Segment& s, int64_t e1, Segment& nx) const {
+    if (s.tile0 + s.ntiles < seq_tiles(s.seqlen)) return false;  // range ended inside the pair
+    return s.pair + 1 < batch * hkv && make(s.pair + 1, 0, e1, nx);
+  }
+};
 
 __device__ __forceinline__ bool lane0_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                            uint64_t budget, int lane) {
@@ -214,9 +291,12 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
   volatile int* last_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 8);
+  // Tiles of this CTA, published by the producer once its walk is done.
+  volatile int* tiles_total = reinterpret_cast<volatile int*>(smem + kOffMisc + 12);
   float* red = reinterpret_cast<float*>(smem + kOffRed);
   float* fin = reinterpret_cast<float*>(smem + kOffFin);
   int* prefix = reinterpret_cast<int*>(smem + kOffPrefix);
+  int* lens = reinterpret_cast<int*>(smem + kOffLens);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -242,6 +322,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     }
     *abort_flag = 0;
     *last_flag = 0;
+    *tiles_total = 0x7fffffff;
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
@@ -255,18 +336,20 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     uint4* z = reinterpret_cast<uint4*>(pbufs);
     for (int i = tid; i < 2 * kPBufBytes / 16; i += kSm100Threads) z[i] = make_uint4(0, 0, 0, 0);
   }
+  const CostModel cm{p.cost_tile, p.cost_seg};
   for (int b = tid; b < batch; b += kSm100Threads) {
     int len = __ldg(p.seqlens + b);
     len = len < 0 ? 0 : len;
-    const int64_t l64 = len > max_len ? max_len : len;
-    prefix[b + 1] = l64 > 0 ? static_cast<int>((l64 + kTileTokens - 1) / kTileTokens) : 1;
+    len = static_cast<int>(len > max_len ? max_len : len);
+    lens[b] = len;
+    prefix[b + 1] = cm.pair_cost(len);
   }
   if (tid == 0) prefix[0] = 0;
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) {  // inclusive scan of tile counts -> exclusive prefix sums
+  if (warp == 0) {  // inclusive scan of pair costs -> exclusive prefix sums
     int carry = 0;
     for (int base = 1; base <= batch; base += 32) {
       const int idx = base + lane;
@@ -285,13 +368,23 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
 
   const uint32_t tmem = *tmem_slot;
   const int cta = blockIdx.x;
-  const int64_t total = static_cast<int64_t>(hkv) * prefix[batch];
-  // The range split uses at most `total` CTAs, so every range is non-empty and
-  // the CTAs cta_of() counts for a pair all hold a segment of it.  CTAs past
-  // that (the host sized the grid from an upper bound) have nothing to do.
-  const int grid = total < static_cast<int64_t>(gridDim.x) ? static_cast<int>(total) : gridDim.x;
-  const int64_t w_begin = cta < grid ? total * cta / grid : 0;
-  const int64_t w_end = cta < grid ? total * (cta + 1) / grid : 0;
+  Schedule sched;
+  sched.cost_prefix = prefix;
+  sched.lens = lens;
+  sched.max_len = max_len;
+  sched.total = static_cast<int64_t>(hkv) * prefix[batch];
+  sched.batch = batch;
+  sched.hkv = hkv;
+  sched.cm = cm;
+  // Each CTA's cost range is longer than the costliest tile (seg + full), so
+  // every range holds at least one tile start: no CTA inside a pair's span is
+  // empty, which the nseg count relies on.  CTAs past that (the host sized
+  // the grid from an upper bound) have nothing to do.
+  {
+    const int64_t g = sched.total / (cm.seg + cm.full() + 1);
+    sched.grid = static_cast<int>(g < 1 ? 1 : (g < gridDim.x ? g : gridDim.x));
+  }
+  const int64_t range_end = sched.range_start(cta + 1);
 
   if (warp == 0) {
     // ---------------------------------------------------------- TMA producer
@@ -308,8 +401,8 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     const int nchunks = kTileTokens / chunk;
     int64_t it = 0;
     bool ok = true;
-    for (int64_t w = w_begin; w < w_end && ok;) {
-      const Segment s = locate(prefix, batch, hkv, total, grid, w, w_end, p.seqlens, max_len);
+    Segment s;
+    for (bool have = sched.first(cta, s); have && ok; have = sched.next(s, range_end, s)) {
       const int32_t* bt_row = p.block_table + static_cast<int64_t>(s.b) * p.bt_stride;
       for (int t = 0; t < s.ntiles; ++t, ++it) {
         const int tok0 = (s.tile0 + t) * kTileTokens;
@@ -348,8 +441,8 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         }
         __syncwarp();
       }
-      w += s.ntiles;
     }
+    if (lane == 0) *tiles_total = static_cast<int>(it);
   } else if (warp == 1) {
     // ---------------------------------------------------------- UMMA issuer
     // Tiles 0 .. ntiles-1 of this CTA's range.  QK(i) needs stage i loaded
@@ -358,14 +451,15 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     constexpr bool kBf16 = DType<T>::kBf16;
     constexpr uint32_t idesc_qk = make_idesc(kBf16, false, false, 128, kMaxGroup);
     constexpr uint32_t idesc_pv = make_idesc(kBf16, true, true, 128, kPvN);
-    const int64_t ntiles = w_end - w_begin;
     int64_t qk = 0, pv = 0;
     uint64_t idle_since = 0;
     uint32_t spins = 0;
-    while (pv < ntiles) {
-      int action = 0;  // 1 = PV, 2 = QK
+    while (true) {
+      int action = 0;  // 1 = PV, 2 = QK, 3 = abort, 4 = all tiles done
       if (lane == 0) {
-        if (pv < qk) {
+        const int64_t ntiles = *tiles_total;  // the producer's count once known
+        if (pv >= ntiles) action = 4;
+        if (action == 0 && pv < qk) {
           const int pb = static_cast<int>(pv & 1);
           const uint32_t ph = static_cast<uint32_t>((pv >> 1) & 1);
           if (mbar_test_wait(&p_full[pb], ph) && mbar_test_wait(&o_empty[pb], ph ^ 1u)) action = 1;
@@ -390,7 +484,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         }
       }
       action = __shfl_sync(0xffffffffu, action, 0);
-      if (action == 3) break;
+      if (action >= 3) break;
       if (action == 0) continue;
       tc_fence_after();
       if (lane == 0) {
@@ -446,8 +540,6 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     const float neg_inf = -__int_as_float(0x7f800000);
     const int hq = p.num_heads;
     OutT* out = reinterpret_cast<OutT*>(p.out);
-    const int64_t ntiles = w_end - w_begin;
-
     struct State {
       float m[NCOL], l[NCOL], o[NCOL], a[NCOL];
     };
@@ -551,15 +643,15 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     reset(cur);
     reset(prev);
     Segment seg{}, prev_seg{};
-    int64_t w = w_begin;
     int t = 0;
-    if (ntiles > 0) seg = locate(prefix, batch, hkv, total, grid, w, w_end, p.seqlens, max_len);
-    for (int64_t it = 0; it < ntiles; ++it, ++t) {
+    int64_t it = 0;
+    for (bool have = sched.first(cta, seg); have; ++it, ++t) {
       bool prev_open = false;
-      if (t == seg.ntiles) {  // next segment
-        w += seg.ntiles;
+      if (t == seg.ntiles) {  // next segment, if the range has one
+        Segment nx;
+        if (!sched.next(seg, range_end, nx)) break;
         prev_seg = seg;
-        seg = locate(prefix, batch, hkv, total, grid, w, w_end, p.seqlens, max_len);
+        seg = nx;
         t = 0;
         prev = cur;
         reset(cur);
@@ -644,9 +736,9 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
 #pragma unroll
       for (int h = 0; h < NCOL; ++h) cur.a[h] = alpha[h];
     }
-    if (ntiles > 0) {
+    if (it > 0) {
       float ov[NCOL];
-      load_o(ntiles - 1, ov);
+      load_o(it - 1, ov);
 #pragma unroll
       for (int h = 0; h < NCOL; ++h) cur.o[h] = fmaf(cur.o[h], cur.a[h], ov[h]);
       finish(seg, cur);

@@ -11,7 +11,7 @@ namespace fd {
 constexpr int kHeadDim = 128;          // head dim of the tensor-core path
 constexpr int kTileTokens = 128;       // KV tokens per pipeline stage (UMMA M of Q.K^T)
 constexpr int kMaxGroup = 16;          // query heads per KV head (UMMA N, padded)
-constexpr int kMaxBatchPerLaunch = 1024;  // sequences per launch (schedule lives in smem)
+constexpr int kMaxBatchPerLaunch = 512;   // sequences per launch (schedule lives in smem)
 constexpr int kSm100Threads = 192;     // warp0 TMA, warp1 MMA, warps2-5 softmax/epilogue
 
 // Per-launch parameters of the tensor-core kernel (tensor maps travel as
@@ -30,6 +30,8 @@ struct DecodeParams {
   int* err;                   // device error word
   unsigned long long timeout_ns;
   uint32_t epoch;             // 1 .. 2^20-1, different for consecutive launches
+  int cost_tile, cost_seg;    // split cost model: fixed cost per tile and per pair, in
+                              // units where a full tile's K/V bytes cost 8
 };
 
 struct SimtParams {

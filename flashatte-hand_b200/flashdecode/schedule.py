@@ -2,17 +2,27 @@
 
 The kernel decides its split on the device from cache_seqlens; this module
 computes the same partition on the host so tests can check its invariants
-(every tile covered once, partial slots unique, balanced ranges) and the
-bench can report split statistics.  It replaces the reference's
-choose_splits table (submission-oj/best_flashattn_kvcache_decode.cu:1039-1076)
-and its per-split page ranges (:664-671).
+(every tile covered once, partial slots unique, no empty CTA inside a pair's
+span) and the bench can report split statistics.  It replaces the
+reference's choose_splits table
+(submission-oj/best_flashattn_kvcache_decode.cu:1039-1076) and its per-split
+page ranges (:664-671).
+
+Cost model (integer units, a full 128-token tile's K/V bytes = 8): a tile
+adds ``tile_fixed``; a sequence's partial last tile costs its 16-token boxes
+instead of 8; every (sequence, KV head) pair adds ``seg``.  Pairs are laid end
+to end (b-major, then KV head) and CTA c takes the tiles whose start cost is
+in [C*c/G, C*(c+1)/G).
 """
 from __future__ import annotations
 
 from dataclasses import dataclass
 
 TILE_TOKENS = 128
-MAX_BATCH_PER_LAUNCH = 1024
+MAX_BATCH_PER_LAUNCH = 512
+FULL_TILE = 8
+DEFAULT_TILE_FIXED = 2
+DEFAULT_SEG = 12
 
 
 @dataclass(frozen=True)
@@ -38,53 +48,92 @@ def tiles_of(length: int, max_len: int | None = None) -> int:
     return (L + TILE_TOKENS - 1) // TILE_TOKENS if L > 0 else 1
 
 
-def cta_of(w: int, total: int, grid: int) -> int:
-    """Largest c with floor(total * c / grid) <= w."""
-    return ((w + 1) * grid + total - 1) // total - 1
+def pair_cost(length: int, tile_fixed: int = DEFAULT_TILE_FIXED, seg: int = DEFAULT_SEG) -> int:
+    L = max(0, int(length))
+    n_full, rem = divmod(L, TILE_TOKENS)
+    tail = ((rem + 15) // 16 + tile_fixed) if (rem > 0 or L == 0) else 0
+    return seg + n_full * (FULL_TILE + tile_fixed) + tail
+
+
+def segments(seqlens, hkv: int, grid: int, max_len: int | None = None,
+             tile_fixed: int = DEFAULT_TILE_FIXED, seg: int = DEFAULT_SEG) -> list[Segment]:
+    """All segments of all CTAs, in CTA order then work order (kernel's split)."""
+    lens = [min(max(0, int(L)), max_len) if max_len is not None else max(0, int(L)) for L in seqlens]
+    full = FULL_TILE + tile_fixed
+    prefix = [0]
+    for L in lens:
+        prefix.append(prefix[-1] + pair_cost(L, tile_fixed, seg))
+    total = hkv * prefix[-1]
+    grid = max(1, min(grid, total // (seg + full + 1)))
+    npairs = len(lens) * hkv
+
+    def range_start(c):
+        return total * c // grid
+
+    def cta_of(s):
+        return ((s + 1) * grid + total - 1) // total - 1
+
+    def pair_start(pair):
+        b, kvh = divmod(pair, hkv)
+        return hkv * prefix[b] + kvh * (prefix[b + 1] - prefix[b])
+
+    def tile_start(cp, j):
+        return cp if j == 0 else cp + seg + j * full
+
+    def make(c, pair, j0, e1):
+        b, kvh = divmod(pair, hkv)
+        n = tiles_of(lens[b])
+        cp = pair_start(pair)
+        if j0 >= n or tile_start(cp, j0) >= e1:
+            return None
+        x = e1 - cp - seg
+        jmax = -(-x // full) - 1 if x > 0 else 0
+        jmax = min(jmax, n - 1)
+        c0 = cta_of(cp)
+        return Segment(c, b, kvh, pair, j0, jmax - j0 + 1, cta_of(tile_start(cp, n - 1)) - c0 + 1, c0)
+
+    out: list[Segment] = []
+    for c in range(grid):
+        e0, e1 = range_start(c), range_start(c + 1)
+        lo, hi = 0, len(lens) - 1
+        while lo < hi:
+            mid = (lo + hi + 1) // 2
+            if hkv * prefix[mid] <= e0:
+                lo = mid
+            else:
+                hi = mid - 1
+        pc = prefix[lo + 1] - prefix[lo]
+        kvh = min(hkv - 1, (e0 - hkv * prefix[lo]) // pc)
+        pair = lo * hkv + kvh
+        cp = pair_start(pair)
+        j0 = 0
+        if e0 > cp:
+            x = e0 - cp - seg
+            j0 = max(1, -(-x // full)) if x > 0 else 1
+        s = make(c, pair, j0, e1)
+        if s is None and pair + 1 < npairs:
+            s = make(c, pair + 1, 0, e1)
+        while s is not None:
+            out.append(s)
+            if s.tile0 + s.ntiles < tiles_of(lens[s.b]) or s.pair + 1 >= npairs:
+                break
+            s = make(c, s.pair + 1, 0, e1)
+    return out
 
 
 def grid_size(batch: int, hkv: int, num_sms: int, tiles_bound: int) -> int:
     return min(num_sms, batch * hkv * tiles_bound)
 
 
-def segments(seqlens, hkv: int, grid: int, max_len: int | None = None) -> list[Segment]:
-    """All segments of all CTAs, in CTA order then work order."""
-    n = [tiles_of(L, max_len) for L in seqlens]
-    prefix = [0]
-    for x in n:
-        prefix.append(prefix[-1] + x)
-    total = hkv * prefix[-1]
-    grid = min(grid, total)  # the kernel never splits over more CTAs than tiles
-    out: list[Segment] = []
-    for c in range(grid):
-        w, w_end = total * c // grid, total * (c + 1) // grid
-        while w < w_end:
-            # largest b with hkv * prefix[b] <= w
-            lo, hi = 0, len(n) - 1
-            while lo < hi:
-                mid = (lo + hi + 1) // 2
-                if hkv * prefix[mid] <= w:
-                    lo = mid
-                else:
-                    hi = mid - 1
-            b = lo
-            r = w - hkv * prefix[b]
-            kvh, tile0 = divmod(r, n[b])
-            pair_start = w - tile0
-            pair_end = pair_start + n[b]
-            seg_end = min(w_end, pair_end)
-            c0, c1 = cta_of(pair_start, total, grid), cta_of(pair_end - 1, total, grid)
-            out.append(Segment(c, b, kvh, b * hkv + kvh, tile0, seg_end - w, c1 - c0 + 1, c0))
-            w = seg_end
-    return out
-
-
-def split_stats(seqlens, hkv: int, grid: int) -> dict:
-    segs = segments(seqlens, hkv, grid)
+def split_stats(seqlens, hkv: int, grid: int, **kw) -> dict:
+    segs = segments(seqlens, hkv, grid, **kw)
+    ctas = max(s.cta for s in segs) + 1
     split_pairs = {s.pair for s in segs if s.nseg > 1}
-    per_cta = [0] * grid
+    per_cta = [0] * ctas
+    seg_cta = [0] * ctas
     for s in segs:
         per_cta[s.cta] += s.ntiles
+        seg_cta[s.cta] += 1
     return dict(segments=len(segs), pairs=len(seqlens) * hkv, split_pairs=len(split_pairs),
-                tiles_total=sum(per_cta), tiles_per_cta_max=max(per_cta),
-                tiles_per_cta_min=min(per_cta))
+                ctas=ctas, tiles_total=sum(per_cta), tiles_per_cta_max=max(per_cta),
+                tiles_per_cta_min=min(per_cta), segments_per_cta_max=max(seg_cta))

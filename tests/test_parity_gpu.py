@@ -162,7 +162,7 @@ def test_batch_larger_than_one_launch():
     c = cases.custom_case("bigbatch", torch.float16, sl, 8, 2, page=16, seed=1)
     t = cases.materialize(c, "cuda", seed=1)
     out, lse = run(t, c, return_softmax_lse=True)
-    check(c, t, out, lse, rows=[0, 1, 1023, 1024, 2047, 2048, 2049, 2499])
+    check(c, t, out, lse, rows=[0, 1, 511, 512, 1023, 1024, 2047, 2048, 2049, 2499])
 
 
 @pytest.mark.parametrize("shape", cases.CONTEST_SHAPES)
