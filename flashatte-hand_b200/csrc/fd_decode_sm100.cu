@@ -14,11 +14,11 @@
 // combine launch, best :956-1037, :1420-1425).
 //
 // Per tile the CTA runs, warp-specialised:
-//   warp 0    TMA producer: gathers the tile's K and V rows page by page
-//             through block_table into a 3-deep shared-memory ring
-//             (128B-swizzled, two 64-dim halves), with the group's query rows
-//             riding in the same stage; a sequence's last, partial tile is
-//             fetched in 16-token boxes covering only its valid rows.
+//   warps 0,6 TMA producers: gather the tile's K (warp 0, with the group's
+//             query rows) and V (warp 6) rows page by page through
+//             block_table into a 3-deep shared-memory ring (128B-swizzled,
+//             two 64-dim halves); a sequence's last, partial tile is fetched
+//             in 16-token boxes covering only its valid rows.
 //   warp 1    tcgen05 issuer: S^T[tok, head] = K . Q^T (M=128 tokens, N=16
 //             heads, K=128 dims) into TMEM, then O^T[dim, head] = V^T . P^T
 //             (M=128 dims, N=2x16 heads, K=128 tokens) into TMEM, each issued
@@ -50,6 +50,7 @@ constexpr int kStageBytes = 2 * kOperandBytes + kQSlotBytes;  // K + V + Q: 68 K
 constexpr int kPBufBytes = kTileTokens * 2 * kMaxGroup * 2;
 constexpr int kTmemCols = 128;                   // S0 S1 (16 cols each), O0 O1 (32 each)
 constexpr int kNumBars = 2 * kStages + 10;
+constexpr int kVProducerWarp = 6;
 
 // Shared-memory carve-up, offsets from a 1024-byte aligned base.
 constexpr int kOffStages = 0;
@@ -281,8 +282,8 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   uint8_t* stages = smem + kOffStages;
   uint8_t* pbufs = smem + kOffP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + kStages;
+  uint64_t* full = bars;            // stage loaded: K, V and query rows (two producers)
+  uint64_t* empty = bars + kStages;  // stage consumed: P.V of its tile done
   uint64_t* s_full = bars + 2 * kStages;
   uint64_t* s_empty = s_full + 2;
   uint64_t* p_full = s_empty + 2;
@@ -310,7 +311,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   // ------------------------------------------------------------ prologue
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 2);
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -386,15 +387,29 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   }
   const int64_t range_end = sched.range_start(cta + 1);
 
-  if (warp == 0) {
-    // ---------------------------------------------------------- TMA producer
+  if (warp == 0 || warp == kVProducerWarp) {
+    // ---------------------------------------------------------- TMA producers
+    // Warp 0 issues the K boxes and the group's query rows of each stage,
+    // warp 6 its V boxes; both arrive on the stage's `full` barrier.  Two
+    // issuing warps halve the per-stage TMA issue time, which matters for
+    // small pages (16-token boxes: 16 per operand per tile).
+    const bool is_v = warp == kVProducerWarp;
     if (lane == 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      tma_prefetch_desc(&tm_k16);
-      tma_prefetch_desc(&tm_v16);
+      if (is_v) {
+        tma_prefetch_desc(&tm_v);
+        tma_prefetch_desc(&tm_v16);
+      } else {
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_k16);
+      }
     }
+    uint64_t* ring_full = full;
+    uint64_t* ring_empty = empty;
+    const CUtensorMap* map_full = is_v ? &tm_v : &tm_k;
+    const CUtensorMap* map_tail = is_v ? &tm_v16 : &tm_k16;
+    const int operand_off = is_v ? kOperandBytes : 0;
+    const uint32_t extra_tx = is_v ? 0u : 2u * group * 128u;  // query rows ride with K
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_keep = policy_evict_last();
     const int chunk = p.chunk;  // tokens per TMA box of a full tile; never crosses a page
@@ -417,32 +432,31 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         int page_id = 0;
         if (need) page_id = __ldg(bt_row + pos / p.page);  // issued before the wait
         const int stage = static_cast<int>(it % kStages);
-        ok = lane0_wait(&empty[stage], static_cast<uint32_t>((it / kStages) & 1) ^ 1u, abort_flag,
-                        budget, lane);
+        ok = lane0_wait(&ring_empty[stage], static_cast<uint32_t>((it / kStages) & 1) ^ 1u,
+                        abort_flag, budget, lane);
         if (!ok) break;
-        uint8_t* kdst = stages + stage * kStageBytes;
+        uint8_t* sdst = stages + stage * kStageBytes;
         if (lane == 0) {
-          mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(nbox * box) * 512u + 2u * group * 128u);
-          uint8_t* qdst = kdst + 2 * kOperandBytes;
-          tma_load_3d(&tm_q, &full[stage], qdst, 0, s.kvh * group, s.b, pol_keep);
-          tma_load_3d(&tm_q, &full[stage], qdst + kQSlotBytes / 2, 64, s.kvh * group, s.b, pol_keep);
+          mbar_arrive_expect_tx(&ring_full[stage], static_cast<uint32_t>(nbox * box) * 256u + extra_tx);
+          if (!is_v) {
+            uint8_t* qdst = sdst + 2 * kOperandBytes;
+            tma_load_3d(&tm_q, &ring_full[stage], qdst, 0, s.kvh * group, s.b, pol_keep);
+            tma_load_3d(&tm_q, &ring_full[stage], qdst + kQSlotBytes / 2, 64, s.kvh * group, s.b,
+                        pol_keep);
+          }
         }
         __syncwarp();
         if (need) {
           const int off = pos % p.page;
-          const CUtensorMap* mk = tail ? &tm_k16 : &tm_k;
-          const CUtensorMap* mv = tail ? &tm_v16 : &tm_v;
-          uint8_t* kd = kdst + lane * box * 128;
-          uint8_t* vd = kd + kOperandBytes;
-          tma_load_4d(mk, &full[stage], kd, 0, s.kvh, off, page_id, pol_stream);
-          tma_load_4d(mk, &full[stage], kd + kHalfBytes, 64, s.kvh, off, page_id, pol_stream);
-          tma_load_4d(mv, &full[stage], vd, 0, s.kvh, off, page_id, pol_stream);
-          tma_load_4d(mv, &full[stage], vd + kHalfBytes, 64, s.kvh, off, page_id, pol_stream);
+          const CUtensorMap* m = tail ? map_tail : map_full;
+          uint8_t* dst = sdst + operand_off + lane * box * 128;
+          tma_load_4d(m, &ring_full[stage], dst, 0, s.kvh, off, page_id, pol_stream);
+          tma_load_4d(m, &ring_full[stage], dst + kHalfBytes, 64, s.kvh, off, page_id, pol_stream);
         }
         __syncwarp();
       }
     }
-    if (lane == 0) *tiles_total = static_cast<int>(it);
+    if (!is_v && lane == 0) *tiles_total = static_cast<int>(it);
   } else if (warp == 1) {
     // ---------------------------------------------------------- UMMA issuer
     // Tiles 0 .. ntiles-1 of this CTA's range.  QK(i) needs stage i loaded

@@ -12,7 +12,7 @@ constexpr int kHeadDim = 128;          // head dim of the tensor-core path
 constexpr int kTileTokens = 128;       // KV tokens per pipeline stage (UMMA M of Q.K^T)
 constexpr int kMaxGroup = 16;          // query heads per KV head (UMMA N, padded)
 constexpr int kMaxBatchPerLaunch = 512;   // sequences per launch (schedule lives in smem)
-constexpr int kSm100Threads = 192;     // warp0 TMA, warp1 MMA, warps2-5 softmax/epilogue
+constexpr int kSm100Threads = 224;     // warps 0/6 TMA, warp 1 MMA, warps 2-5 softmax/epilogue
 
 // Per-launch parameters of the tensor-core kernel (tensor maps travel as
 // separate __grid_constant__ arguments).
