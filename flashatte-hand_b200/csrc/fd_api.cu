@@ -207,9 +207,10 @@ const char* fd_error_string(int code) {
   }
 }
 
-size_t fd_decode_workspace_size(int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
-                                int64_t headdim) {
-  if (batch_size <= 0 || num_heads <= 0 || num_heads_k <= 0 || num_heads % num_heads_k != 0)
+size_t fd_decode_workspace_size_mq(int64_t batch_size, int64_t seqlen_q, int64_t num_heads,
+                                   int64_t num_heads_k, int64_t headdim) {
+  if (batch_size <= 0 || seqlen_q <= 0 || num_heads <= 0 || num_heads_k <= 0 ||
+      num_heads % num_heads_k != 0)
     return 0;
   (void)headdim;
   int dev = 0;
@@ -217,20 +218,26 @@ size_t fd_decode_workspace_size(int64_t batch_size, int64_t num_heads, int64_t n
   const int sms = device_sms(dev);
   if (sms <= 0) return 0;
   const int64_t nb = batch_size < fd::kMaxBatchPerLaunch ? batch_size : fd::kMaxBatchPerLaunch;
-  return fd::workspace_layout(nb, num_heads_k, num_heads / num_heads_k, sms).total;
+  return fd::workspace_layout(nb, num_heads_k, seqlen_q * (num_heads / num_heads_k), sms).total;
 }
 
-int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, void* out, float* lse,
-                    const int32_t* cache_seqlens, const int32_t* block_table,
-                    int64_t block_table_stride, int64_t batch_size, int64_t num_heads,
-                    int64_t num_heads_k, int64_t headdim, int64_t page_block_size,
-                    int64_t num_blocks, int dtype, int out_dtype, float softmax_scale,
-                    int64_t max_seqlen_k, void* workspace, size_t workspace_bytes, void* stream) {
+size_t fd_decode_workspace_size(int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
+                                int64_t headdim) {
+  return fd_decode_workspace_size_mq(batch_size, 1, num_heads, num_heads_k, headdim);
+}
+
+int fd_decode_paged_mq(const void* q, const void* k_cache, const void* v_cache, void* out,
+                       float* lse, const int32_t* cache_seqlens, const int32_t* block_table,
+                       int64_t block_table_stride, int64_t batch_size, int64_t seqlen_q,
+                       int64_t num_heads, int64_t num_heads_k, int64_t headdim,
+                       int64_t page_block_size, int64_t num_blocks, int dtype, int out_dtype,
+                       float softmax_scale, int causal, int64_t max_seqlen_k, void* workspace,
+                       size_t workspace_bytes, void* stream) {
   if (q == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr ||
       cache_seqlens == nullptr || block_table == nullptr)
     return set_error(FD_ERR_INVALID_ARG, "null tensor pointer");
-  if (batch_size <= 0 || num_heads <= 0 || num_heads_k <= 0 || page_block_size <= 0 ||
-      num_blocks <= 0 || block_table_stride <= 0)
+  if (batch_size <= 0 || seqlen_q <= 0 || num_heads <= 0 || num_heads_k <= 0 ||
+      page_block_size <= 0 || num_blocks <= 0 || block_table_stride <= 0)
     return set_error(FD_ERR_INVALID_ARG,
                      "sizes must be positive (batch=%lld heads=%lld kv_heads=%lld page=%lld "
                      "num_blocks=%lld bt_stride=%lld)",
@@ -249,7 +256,7 @@ int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, voi
   if (headdim != 32 && headdim != 64 && headdim != 128 && headdim != 256)
     return set_error(FD_ERR_UNSUPPORTED, "head dim %lld not in {32, 64, 128, 256}",
                      (long long)headdim);
-  if (batch_size * num_heads > INT32_MAX || num_blocks > INT32_MAX ||
+  if (batch_size * seqlen_q * num_heads > INT32_MAX || seqlen_q > 65535 || num_blocks > INT32_MAX ||
       page_block_size > INT32_MAX || num_heads > 65535)
     return set_error(FD_ERR_UNSUPPORTED, "size exceeds 32-bit index range");
 
@@ -261,8 +268,9 @@ int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, voi
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
   const bool out_fp32 = out_dtype == FD_DTYPE_FP32;
   const int chunk = pick_chunk(page_block_size);
+  const int64_t qrows = seqlen_q * group;
 
-  const bool tensor_core_path = headdim == fd::kHeadDim && group <= fd::kMaxGroup && chunk > 0 &&
+  const bool tensor_core_path = headdim == fd::kHeadDim && qrows <= fd::kMaxGroup && chunk > 0 &&
                                 aligned16(q) && aligned16(k_cache) && aligned16(v_cache) &&
                                 encode_fn() != nullptr;
   if (!tensor_core_path) {
@@ -272,6 +280,7 @@ int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, voi
     sp.batch = static_cast<int>(batch_size); sp.num_heads = static_cast<int>(num_heads);
     sp.num_heads_k = static_cast<int>(num_heads_k); sp.group = group;
     sp.head_dim = static_cast<int>(headdim); sp.page = static_cast<int>(page_block_size);
+    sp.seqlen_q = static_cast<int>(seqlen_q); sp.causal = causal ? 1 : 0;
     sp.num_blocks = num_blocks; sp.scale_log2 = scale_log2;
     const int vec = static_cast<int>(headdim / 32) * 2;  // bytes per lane load
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_cache) |
@@ -285,7 +294,7 @@ int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, voi
   const int sms = device_sms(dev);
   if (sms <= 0) return set_error(FD_ERR_CUDA, "cannot query SM count");
   const int64_t nb_max = batch_size < fd::kMaxBatchPerLaunch ? batch_size : fd::kMaxBatchPerLaunch;
-  const fd::WorkspaceLayout wl = fd::workspace_layout(nb_max, num_heads_k, group, sms);
+  const fd::WorkspaceLayout wl = fd::workspace_layout(nb_max, num_heads_k, qrows, sms);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (ws == nullptr) {
     ws = static_cast<uint8_t*>(internal_workspace(dev, wl.total, st));
@@ -329,16 +338,18 @@ int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, voi
   for (int64_t b0 = 0; b0 < batch_size; b0 += per_launch) {
     const int64_t nb = batch_size - b0 < per_launch ? batch_size - b0 : per_launch;
     {
-      const uint8_t* qb = static_cast<const uint8_t*>(q) + b0 * num_heads * 128 * es;
-      const cuuint64_t dims[3] = {128, (cuuint64_t)num_heads, (cuuint64_t)nb};
-      const cuuint64_t strides[2] = {(cuuint64_t)(128 * es), (cuuint64_t)(num_heads * 128 * es)};
-      const cuuint32_t box[3] = {64, (cuuint32_t)group, 1};
-      const CUresult r = encode(&maps.q, dtype, 3, qb, dims, strides, box);
+      // q [nb, sq, Hq, 128]: box = 64 dims x group heads x all sq tokens of one sequence
+      const uint8_t* qb = static_cast<const uint8_t*>(q) + b0 * seqlen_q * num_heads * 128 * es;
+      const cuuint64_t dims[4] = {128, (cuuint64_t)num_heads, (cuuint64_t)seqlen_q, (cuuint64_t)nb};
+      const cuuint64_t strides[3] = {(cuuint64_t)(128 * es), (cuuint64_t)(num_heads * 128 * es),
+                                     (cuuint64_t)(seqlen_q * num_heads * 128 * es)};
+      const cuuint32_t box[4] = {64, (cuuint32_t)group, (cuuint32_t)seqlen_q, 1};
+      const CUresult r = encode(&maps.q, dtype, 4, qb, dims, strides, box);
       if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "Q tensor map encode failed (%d)", (int)r);
     }
     fd::DecodeParams p;
-    p.out = static_cast<uint8_t*>(out) + b0 * num_heads * 128 * esize(out_dtype);
-    p.lse = lse != nullptr ? lse + b0 * num_heads : nullptr;
+    p.out = static_cast<uint8_t*>(out) + b0 * seqlen_q * num_heads * 128 * esize(out_dtype);
+    p.lse = lse != nullptr ? lse + b0 * num_heads * seqlen_q : nullptr;
     p.seqlens = cache_seqlens + b0;
     p.block_table = block_table + b0 * block_table_stride;
     p.bt_stride = block_table_stride;
@@ -346,6 +357,9 @@ int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, voi
     p.num_heads = static_cast<int>(num_heads);
     p.num_heads_k = static_cast<int>(num_heads_k);
     p.group = group;
+    p.seqlen_q = static_cast<int>(seqlen_q);
+    p.causal = causal ? 1 : 0;
+    p.qrows = static_cast<int>(qrows);
     p.page = static_cast<int>(page_block_size);
     p.chunk = chunk;
     p.scale_log2 = scale_log2;
@@ -365,16 +379,23 @@ int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, voi
   return set_ok();
 }
 
+int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, void* out, float* lse,
+                    const int32_t* cache_seqlens, const int32_t* block_table,
+                    int64_t block_table_stride, int64_t batch_size, int64_t num_heads,
+                    int64_t num_heads_k, int64_t headdim, int64_t page_block_size,
+                    int64_t num_blocks, int dtype, int out_dtype, float softmax_scale,
+                    int64_t max_seqlen_k, void* workspace, size_t workspace_bytes, void* stream) {
+  return fd_decode_paged_mq(q, k_cache, v_cache, out, lse, cache_seqlens, block_table,
+                            block_table_stride, batch_size, 1, num_heads, num_heads_k, headdim,
+                            page_block_size, num_blocks, dtype, out_dtype, softmax_scale, 0,
+                            max_seqlen_k, workspace, workspace_bytes, stream);
+}
+
 void run_kernel(const void* q, const void* k_cache_paged, const void* v_cache_paged, void* output,
                 const int32_t* cache_seqlens, const int32_t* block_table, int64_t batch_size,
                 int64_t seqlen_k, int64_t seqlen_q, int64_t num_heads, int64_t num_heads_k,
                 int64_t headdim, int64_t page_block_size, int64_t num_blocks, int64_t causal) {
-  (void)causal;  // one query token: the causal mask admits every cached key
-  if (seqlen_q != 1) {
-    set_error(FD_ERR_UNSUPPORTED, "seqlen_q=%lld: only single-token decode", (long long)seqlen_q);
-    return;
-  }
-  if (batch_size <= 0 || num_blocks <= 0 || headdim <= 0) {
+  if (batch_size <= 0 || num_blocks <= 0 || headdim <= 0 || seqlen_q <= 0) {
     set_error(FD_ERR_INVALID_ARG, "batch_size, num_blocks and headdim must be positive");
     return;
   }
@@ -385,9 +406,10 @@ void run_kernel(const void* q, const void* k_cache_paged, const void* v_cache_pa
     return;
   }
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(headdim)));
-  fd_decode_paged(q, k_cache_paged, v_cache_paged, output, nullptr, cache_seqlens, block_table,
-                  bt_stride, batch_size, num_heads, num_heads_k, headdim, page_block_size,
-                  num_blocks, FD_DTYPE_BF16, FD_DTYPE_BF16, scale, seqlen_k, nullptr, 0, nullptr);
+  fd_decode_paged_mq(q, k_cache_paged, v_cache_paged, output, nullptr, cache_seqlens, block_table,
+                     bt_stride, batch_size, seqlen_q, num_heads, num_heads_k, headdim,
+                     page_block_size, num_blocks, FD_DTYPE_BF16, FD_DTYPE_BF16, scale,
+                     causal != 0 ? 1 : 0, seqlen_k, nullptr, 0, nullptr);
 }
 
 int fd_combine_lse(const float* part_o, int64_t part_o_stride, const float* part_lse,

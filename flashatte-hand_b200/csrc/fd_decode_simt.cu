@@ -44,9 +44,11 @@ __global__ void __launch_bounds__(32 * kSimtWarps)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
-  const int b = bh / p.num_heads;
-  const int h = bh - b * p.num_heads;
+  const int bqh = blockIdx.x;  // (b, qi, h), h fastest: q/out row index
+  const int h = bqh % p.num_heads;
+  const int bq = bqh / p.num_heads;
+  const int qi = bq % p.seqlen_q;
+  const int b = bq / p.seqlen_q;
   const int kvh = h / p.group;
   const float neg_inf = -__int_as_float(0x7f800000);
 
@@ -54,8 +56,11 @@ __global__ void __launch_bounds__(32 * kSimtWarps)
   len = len < 0 ? 0 : len;
   const int64_t max_len = p.bt_stride * static_cast<int64_t>(p.page);
   if (len > max_len) len = static_cast<int>(max_len);
+  // bottom-right causal mask: query token qi sits at position L - sq + qi
+  if (p.causal) len = len - (p.seqlen_q - 1 - qi);
+  if (len < 0) len = 0;
 
-  const T* q = reinterpret_cast<const T*>(p.q) + static_cast<int64_t>(bh) * D + lane * VEC;
+  const T* q = reinterpret_cast<const T*>(p.q) + static_cast<int64_t>(bqh) * D + lane * VEC;
   const T* kc = reinterpret_cast<const T*>(p.k);
   const T* vc = reinterpret_cast<const T*>(p.v);
   const int32_t* bt = p.block_table + static_cast<int64_t>(b) * p.bt_stride;
@@ -111,7 +116,7 @@ __global__ void __launch_bounds__(32 * kSimtWarps)
     wts[w] = sm_m[w] == neg_inf ? 0.f : fast_exp2(sm_m[w] - mx);
     den = fmaf(wts[w], sm_l[w], den);
   }
-  OutT* out = reinterpret_cast<OutT*>(p.out) + static_cast<int64_t>(bh) * D;
+  OutT* out = reinterpret_cast<OutT*>(p.out) + static_cast<int64_t>(bqh) * D;
   for (int d = threadIdx.x; d < D; d += 32 * kSimtWarps) {
     float o = 0.f;
 #pragma unroll
@@ -119,7 +124,8 @@ __global__ void __launch_bounds__(32 * kSimtWarps)
     out[d] = from_f32<OutT>(den > 0.f ? o / den : 0.f);
   }
   if (p.lse != nullptr && threadIdx.x == 0)
-    p.lse[bh] = den > 0.f ? (mx + fast_log2(den)) * 0.69314718055994531f : neg_inf;
+    p.lse[(static_cast<int64_t>(b) * p.num_heads + h) * p.seqlen_q + qi] =
+        den > 0.f ? (mx + fast_log2(den)) * 0.69314718055994531f : neg_inf;
 }
 
 // out[r] = sum_j w_j o_j[r] / sum_j w_j with w_j = exp(lse_j - max lse),
@@ -155,7 +161,7 @@ __global__ void __launch_bounds__(128)
 
 template <typename T, typename OutT>
 cudaError_t launch_simt_typed(const SimtParams& p, cudaStream_t stream) {
-  const int grid = p.batch * p.num_heads;
+  const int grid = p.batch * p.seqlen_q * p.num_heads;
   switch (p.head_dim) {
     case 32: decode_simt_kernel<T, OutT, 1><<<grid, 32 * kSimtWarps, 0, stream>>>(p); break;
     case 64: decode_simt_kernel<T, OutT, 2><<<grid, 32 * kSimtWarps, 0, stream>>>(p); break;

@@ -264,7 +264,9 @@ __device__ __forceinline__ bool lane0_wait(uint64_t* bar, uint32_t parity, volat
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-template <typename T, typename OutT, int NCOL>
+// MULTI = false: one query token per sequence, no causal mask (plain decode).
+// MULTI = true: seqlen_q query tokens, optional bottom-right causal mask.
+template <typename T, typename OutT, int NCOL, bool MULTI>
 __global__ void __launch_bounds__(kSm100Threads, 1)
     decode_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
@@ -305,6 +307,8 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   const int batch = p.batch;
   const int hkv = p.num_heads_k;
   const int group = p.group;
+  const int sq = MULTI ? p.seqlen_q : 1;  // query tokens per sequence
+  const int qrows = p.qrows;   // query rows per (sequence, KV head): sq * group <= 16
   const uint64_t budget = p.timeout_ns;
   const int64_t max_len = p.bt_stride * static_cast<int64_t>(p.page);
 
@@ -327,8 +331,8 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
-  // Zero the stages' query areas (rows >= group stay zero: the query TMA
-  // writes rows < group only) and the P buffers (heads >= group stay zero).
+  // Zero the stages' query areas (rows >= qrows stay zero: the query TMA
+  // writes rows < qrows only) and the P buffers (columns >= qrows stay zero).
   for (int s = 0; s < kStages; ++s) {
     uint4* z = reinterpret_cast<uint4*>(stages + s * kStageBytes + 2 * kOperandBytes);
     for (int i = tid; i < kQSlotBytes / 16; i += kSm100Threads) z[i] = make_uint4(0, 0, 0, 0);
@@ -409,7 +413,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     const CUtensorMap* map_full = is_v ? &tm_v : &tm_k;
     const CUtensorMap* map_tail = is_v ? &tm_v16 : &tm_k16;
     const int operand_off = is_v ? kOperandBytes : 0;
-    const uint32_t extra_tx = is_v ? 0u : 2u * group * 128u;  // query rows ride with K
+    const uint32_t extra_tx = is_v ? 0u : 2u * qrows * 128u;  // query rows ride with K
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_keep = policy_evict_last();
     const int chunk = p.chunk;  // tokens per TMA box of a full tile; never crosses a page
@@ -440,8 +444,9 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
           mbar_arrive_expect_tx(&ring_full[stage], static_cast<uint32_t>(nbox * box) * 256u + extra_tx);
           if (!is_v) {
             uint8_t* qdst = sdst + 2 * kOperandBytes;
-            tma_load_3d(&tm_q, &ring_full[stage], qdst, 0, s.kvh * group, s.b, pol_keep);
-            tma_load_3d(&tm_q, &ring_full[stage], qdst + kQSlotBytes / 2, 64, s.kvh * group, s.b,
+            // rows qi * group + g: query token qi, head kvh * group + g
+            tma_load_4d(&tm_q, &ring_full[stage], qdst, 0, s.kvh * group, 0, s.b, pol_keep);
+            tma_load_4d(&tm_q, &ring_full[stage], qdst + kQSlotBytes / 2, 64, s.kvh * group, 0, s.b,
                         pol_keep);
           }
         }
@@ -596,28 +601,36 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
 #pragma unroll
       for (int h = 0; h < NCOL; ++h)
         l_tot[h] = (fb[h] + fb[kMaxGroup + h]) + (fb[2 * kMaxGroup + h] + fb[3 * kMaxGroup + h]);
+      // column h = query row (qi, g): token qi of the sequence's sq new
+      // tokens, query head kvh * group + g
+      auto out_index = [&](int h) {
+        const int qi = MULTI ? h / group : 0, g = h - qi * group;
+        return ((static_cast<int64_t>(sg.b) * sq + qi) * hq + sg.kvh * group + g) * kHeadDim + d;
+      };
+      auto lse_index = [&](int h) {
+        const int qi = MULTI ? h / group : 0, g = h - qi * group;
+        return (static_cast<int64_t>(sg.b) * hq + sg.kvh * group + g) * sq + qi;
+      };
       if (sg.nseg == 1) {
-        const int64_t obase = (static_cast<int64_t>(sg.b) * hq + sg.kvh * group) * kHeadDim + d;
 #pragma unroll
         for (int h = 0; h < NCOL; ++h) {
-          if (h < group) {
+          if (h < qrows) {
             const float v = l_tot[h] > 0.f ? st.o[h] / l_tot[h] : 0.f;
-            out[obase + static_cast<int64_t>(h) * kHeadDim] = to_out<OutT>(v);
-            if (p.lse != nullptr && d == h) {
-              p.lse[static_cast<int64_t>(sg.b) * hq + sg.kvh * group + h] =
+            out[out_index(h)] = to_out<OutT>(v);
+            if (p.lse != nullptr && d == h)
+              p.lse[lse_index(h)] =
                   l_tot[h] > 0.f ? (st.m[h] + fast_log2(l_tot[h])) * 0.69314718055994531f : neg_inf;
-            }
           }
         }
         return;
       }
       const int64_t slot = static_cast<int64_t>(cta) + sg.pair;
-      float* po = p.part_o + slot * group * kHeadDim + d;
+      float* po = p.part_o + slot * qrows * kHeadDim + d;
 #pragma unroll
       for (int h = 0; h < NCOL; ++h) {
-        if (h < group) {
+        if (h < qrows) {
           po[h * kHeadDim] = l_tot[h] > 0.f ? st.o[h] / l_tot[h] : 0.f;
-          if (d == h) p.part_lse[slot * group + h] = l_tot[h] > 0.f ? st.m[h] + fast_log2(l_tot[h]) : neg_inf;
+          if (d == h) p.part_lse[slot * qrows + h] = l_tot[h] > 0.f ? st.m[h] + fast_log2(l_tot[h]) : neg_inf;
         }
       }
       __threadfence();
@@ -633,25 +646,29 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       if (!merge) return;
       __threadfence();
       const int64_t sbase = static_cast<int64_t>(sg.cfirst) + sg.pair;
-      for (int h = 0; h < group; ++h) {
+      for (int h = 0; h < qrows; ++h) {
         float mx = neg_inf;
-        for (int j = 0; j < sg.nseg; ++j) mx = fmaxf(mx, __ldcg(p.part_lse + (sbase + j) * group + h));
+        for (int j = 0; j < sg.nseg; ++j) mx = fmaxf(mx, __ldcg(p.part_lse + (sbase + j) * qrows + h));
         float den = 0.f, acc = 0.f;
         for (int j = 0; j < sg.nseg; ++j) {
-          const float lj = __ldcg(p.part_lse + (sbase + j) * group + h);
+          const float lj = __ldcg(p.part_lse + (sbase + j) * qrows + h);
           const float wj = lj == neg_inf ? 0.f : fast_exp2(lj - mx);
           if (wj > 0.f) {
-            acc = fmaf(wj, __ldcg(p.part_o + ((sbase + j) * group + h) * kHeadDim + d), acc);
+            acc = fmaf(wj, __ldcg(p.part_o + ((sbase + j) * qrows + h) * kHeadDim + d), acc);
             den += wj;
           }
         }
-        const int64_t oidx = (static_cast<int64_t>(sg.b) * hq + sg.kvh * group + h) * kHeadDim + d;
-        out[oidx] = to_out<OutT>(den > 0.f ? acc / den : 0.f);
+        out[out_index(h)] = to_out<OutT>(den > 0.f ? acc / den : 0.f);
         if (p.lse != nullptr && d == 0)
-          p.lse[static_cast<int64_t>(sg.b) * hq + sg.kvh * group + h] =
-              den > 0.f ? (mx + fast_log2(den)) * 0.69314718055994531f : neg_inf;
+          p.lse[lse_index(h)] = den > 0.f ? (mx + fast_log2(den)) * 0.69314718055994531f : neg_inf;
       }
     };
+
+    // Per query row h = (qi, g): how many of the sequence's last keys it may
+    // not see (0 unless causal): key t is visible iff t < L + coff[h].
+    int coff[NCOL];
+#pragma unroll
+    for (int h = 0; h < NCOL; ++h) coff[h] = (MULTI && p.causal) ? (h / group) - (sq - 1) : 0;
 
     State cur, prev;
     reset(cur);
@@ -689,7 +706,9 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       float* red_t = red + (it & 1) * (4 * kMaxGroup);
 #pragma unroll
       for (int h = 0; h < NCOL; ++h) {
-        sv[h] = valid ? __uint_as_float(r[h]) * p.scale_log2 : neg_inf;
+        // causal: query row h sees keys up to its own position L - sq + qi
+        const bool vis = MULTI ? row < valid_rows + coff[h] : valid;
+        sv[h] = vis ? __uint_as_float(r[h]) * p.scale_log2 : neg_inf;
         const float wm = warp_max_f32(sv[h]);
         if (lane == 0) red_t[quad * kMaxGroup + h] = wm;
       }
@@ -702,7 +721,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         const float m_new = fmaxf(cur.m[h], tmax);
         const float m_use = m_new == neg_inf ? 0.f : m_new;
         alpha[h] = fast_exp2(cur.m[h] - m_use);
-        pv[h] = (h < group) ? fast_exp2(sv[h] - m_use) : 0.f;
+        pv[h] = (h < qrows) ? fast_exp2(sv[h] - m_use) : 0.f;
         cur.l[h] = fmaf(cur.l[h], alpha[h], pv[h]);
         cur.m[h] = m_new;
       }
@@ -779,9 +798,9 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   }
 }
 
-template <typename T, typename OutT, int NCOL>
+template <typename T, typename OutT, int NCOL, bool MULTI>
 cudaError_t launch_typed(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream) {
-  auto kern = decode_sm100_kernel<T, OutT, NCOL>;
+  auto kern = decode_sm100_kernel<T, OutT, NCOL, MULTI>;
   // The attribute is per device; setting it again is harmless.
   static unsigned long long configured = 0;
   int dev = 0;
@@ -799,15 +818,19 @@ cudaError_t launch_typed(const TensorMaps& m, const DecodeParams& p, int grid, c
 
 template <typename T, typename OutT>
 cudaError_t launch_ncol(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream) {
-  if (p.group <= 8) return launch_typed<T, OutT, 8>(m, p, grid, stream);
-  return launch_typed<T, OutT, 16>(m, p, grid, stream);
+  const bool multi = p.seqlen_q > 1 || p.causal;
+  if (p.qrows <= 8)
+    return multi ? launch_typed<T, OutT, 8, true>(m, p, grid, stream)
+                 : launch_typed<T, OutT, 8, false>(m, p, grid, stream);
+  return multi ? launch_typed<T, OutT, 16, true>(m, p, grid, stream)
+               : launch_typed<T, OutT, 16, false>(m, p, grid, stream);
 }
 
 }  // namespace
 
 size_t sm100_smem_bytes() { return static_cast<size_t>(kSmemBytes); }
 
-WorkspaceLayout workspace_layout(int64_t batch_per_launch, int64_t num_heads_k, int64_t group,
+WorkspaceLayout workspace_layout(int64_t batch_per_launch, int64_t num_heads_k, int64_t qrows,
                                  int grid_max) {
   auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
   const size_t pairs = static_cast<size_t>(batch_per_launch * num_heads_k);
@@ -816,8 +839,8 @@ WorkspaceLayout workspace_layout(int64_t batch_per_launch, int64_t num_heads_k, 
   w.err_off = 0;
   w.tickets_off = 256;
   w.lse_off = w.tickets_off + up(pairs * 4);
-  w.o_off = w.lse_off + up(slots * group * 4);
-  w.total = w.o_off + up(slots * group * kHeadDim * 4);
+  w.o_off = w.lse_off + up(slots * qrows * 4);
+  w.total = w.o_off + up(slots * qrows * kHeadDim * 4);
   return w;
 }
 

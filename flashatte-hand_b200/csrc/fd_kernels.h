@@ -17,12 +17,14 @@ constexpr int kSm100Threads = 224;     // warps 0/6 TMA, warp 1 MMA, warps 2-5 s
 // Per-launch parameters of the tensor-core kernel (tensor maps travel as
 // separate __grid_constant__ arguments).
 struct DecodeParams {
-  void* out;                  // [B, Hq, 128] of OutT
-  float* lse;                 // [B, Hq] natural log, nullable
+  void* out;                  // [B, seqlen_q, Hq, 128] of OutT
+  float* lse;                 // [B, Hq, seqlen_q] natural log, nullable
   const int32_t* seqlens;     // [B]
   const int32_t* block_table; // [B, bt_stride]
   int64_t bt_stride;
   int batch, num_heads, num_heads_k, group, page, chunk;
+  int seqlen_q, causal;       // query tokens per sequence; bottom-right causal mask
+  int qrows;                  // seqlen_q * group query rows per (sequence, KV head)
   float scale_log2;           // softmax_scale * log2(e)
   float* part_o;              // [slots, group, 128] fp32 (normalised partial O)
   float* part_lse;            // [slots, group] log2-domain partial LSE
@@ -40,6 +42,7 @@ struct SimtParams {
   const int32_t* seqlens; const int32_t* block_table;
   int64_t bt_stride;
   int batch, num_heads, num_heads_k, group, head_dim, page;
+  int seqlen_q, causal;
   int64_t num_blocks;
   float scale_log2;
 };
@@ -48,10 +51,10 @@ struct SimtParams {
 struct WorkspaceLayout {
   size_t err_off, tickets_off, lse_off, o_off, total;
 };
-WorkspaceLayout workspace_layout(int64_t batch_per_launch, int64_t num_heads_k, int64_t group,
+WorkspaceLayout workspace_layout(int64_t batch_per_launch, int64_t num_heads_k, int64_t qrows,
                                  int grid_max);
 
-// TMA descriptors of one launch: q rows [B, Hq, 128] (box 64 x group), K and
+// TMA descriptors of one launch: q [B, sq, Hq, 128] (box 64 x group x sq), K and
 // V caches [num_blocks, page, Hkv, 128] with `chunk`-token boxes for full
 // tiles and 16-token boxes for a sequence's last partial tile.
 struct TensorMaps {

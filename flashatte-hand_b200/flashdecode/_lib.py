@@ -21,6 +21,9 @@ SIGNATURES: dict[str, tuple] = {
     "run_kernel": (None, [_vp, _vp, _vp, _vp, _vp, _vp] + [_i64] * 9),
     "fd_decode_paged": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp] + [_i64] * 7
                         + [_i32, _i32, _f32, _i64, _vp, _sz, _vp]),
+    "fd_decode_paged_mq": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp] + [_i64] * 8
+                           + [_i32, _i32, _f32, _i32, _i64, _vp, _sz, _vp]),
+    "fd_decode_workspace_size_mq": (_sz, [_i64, _i64, _i64, _i64, _i64]),
     "fd_decode_paged_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp] + [_i64] * 7
                                 + [_i32, _i32, _f32, _i64, _vp]),
     "fd_decode_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),

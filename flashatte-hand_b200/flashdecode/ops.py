@@ -57,8 +57,10 @@ def device_status() -> int:
     return int(load_library().fd_device_status())
 
 
-def workspace_size(batch_size: int, num_heads: int, num_heads_k: int, headdim: int = 128) -> int:
-    return int(load_library().fd_decode_workspace_size(batch_size, num_heads, num_heads_k, headdim))
+def workspace_size(batch_size: int, num_heads: int, num_heads_k: int, headdim: int = 128,
+                   seqlen_q: int = 1) -> int:
+    return int(load_library().fd_decode_workspace_size_mq(batch_size, seqlen_q, num_heads,
+                                                          num_heads_k, headdim))
 
 
 def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
@@ -66,19 +68,22 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                  softmax_scale: float | None = None, return_softmax_lse: bool = False,
                  out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
                  max_seqlen_k: int | None = None, workspace: torch.Tensor | None = None,
-                 stream: torch.cuda.Stream | None = None, lse: torch.Tensor | None = None):
-    """Single-token paged decode attention.
+                 stream: torch.cuda.Stream | None = None, lse: torch.Tensor | None = None,
+                 causal: bool = False):
+    """Paged decode attention for seqlen_q >= 1 query tokens per sequence.
 
-    q [B, 1, Hq, D]; k_cache/v_cache [num_blocks, page, Hkv, D];
+    q [B, sq, Hq, D]; k_cache/v_cache [num_blocks, page, Hkv, D];
     cache_seqlens [B] int32; block_table [B, max_blocks] int32.
-    Returns out [B, 1, Hq, D] (and lse [B, Hq] fp32, natural log).  `out` and
-    `lse` may be given as preallocated contiguous buffers; passing `lse`
-    implies return_softmax_lse.
+    Returns out [B, sq, Hq, D] (and lse fp32 natural log: [B, Hq] for sq = 1,
+    else [B, Hq, sq]).  causal: query token i sits at position
+    cache_seqlens[b] - sq + i and sees keys up to it.  `out` and `lse` may be
+    given as preallocated contiguous buffers; passing `lse` implies
+    return_softmax_lse.
     """
     lib = load_library()
     _require_cuda(q, k_cache, v_cache, cache_seqlens, block_table)
-    if q.dim() != 4 or q.shape[1] != 1:
-        raise ValueError(f"q must be [B, 1, Hq, D], got {tuple(q.shape)}")
+    if q.dim() != 4:
+        raise ValueError(f"q must be [B, seqlen_q, Hq, D], got {tuple(q.shape)}")
     if q.dtype not in _DTYPES or k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
         raise ValueError("q, k_cache, v_cache must share dtype bf16 or fp16")
     if cache_seqlens.dtype != torch.int32 or block_table.dtype != torch.int32:
@@ -87,7 +92,7 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                     ("cache_seqlens", cache_seqlens), ("block_table", block_table)):
         if not t.is_contiguous():
             raise ValueError(f"{name} must be contiguous")
-    B, _, Hq, D = q.shape
+    B, sq, Hq, D = q.shape
     num_blocks, page, Hkv, Dk = k_cache.shape
     if tuple(v_cache.shape) != tuple(k_cache.shape) or Dk != D:
         raise ValueError("k_cache/v_cache shape mismatch")
@@ -96,25 +101,26 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
     odt = q.dtype if out_dtype is None else out_dtype
     if out is None:
-        out = torch.empty((B, 1, Hq, D), dtype=odt, device=q.device)
-    elif out.dtype != odt or tuple(out.shape) != (B, 1, Hq, D) or not out.is_contiguous():
+        out = torch.empty((B, sq, Hq, D), dtype=odt, device=q.device)
+    elif out.dtype != odt or tuple(out.shape) != (B, sq, Hq, D) or not out.is_contiguous():
         raise ValueError("out has the wrong shape, dtype or layout")
+    lse_shape = (B, Hq) if sq == 1 else (B, Hq, sq)
     if lse is not None:
-        if lse.dtype != torch.float32 or tuple(lse.shape) != (B, Hq) or not lse.is_contiguous():
-            raise ValueError("lse must be a contiguous fp32 [B, Hq] tensor")
+        if lse.dtype != torch.float32 or lse.numel() != B * Hq * sq or not lse.is_contiguous():
+            raise ValueError(f"lse must be a contiguous fp32 {lse_shape} tensor")
         return_softmax_lse = True
     elif return_softmax_lse:
-        lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
+        lse = torch.empty(lse_shape, dtype=torch.float32, device=q.device)
     ws_ptr, ws_bytes = None, 0
     if workspace is not None:
         ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     st = stream if stream is not None else torch.cuda.current_stream(q.device)
     with torch.cuda.device(q.device):
-        status = lib.fd_decode_paged(
+        status = lib.fd_decode_paged_mq(
             _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out), _ptr(lse), _ptr(cache_seqlens),
-            _ptr(block_table), int(block_table.shape[1]), B, Hq, Hkv, D, page, num_blocks,
-            _DTYPES[q.dtype], _OUT_DTYPES[odt], scale, int(max_seqlen_k or 0), ws_ptr, ws_bytes,
-            st.cuda_stream)
+            _ptr(block_table), int(block_table.shape[1]), B, sq, Hq, Hkv, D, page, num_blocks,
+            _DTYPES[q.dtype], _OUT_DTYPES[odt], scale, 1 if causal else 0, int(max_seqlen_k or 0),
+            ws_ptr, ws_bytes, st.cuda_stream)
     check(status)
     return (out, lse) if return_softmax_lse else out
 

@@ -52,9 +52,9 @@ extern "C" {
  * on arguments it rejects; unlike the reference the reason is kept and can be
  * read with fd_last_error().  Unsupported-by-the-reference shapes (any head
  * group, page sizes other than 16, fp16 is not reachable here) are computed
- * rather than rejected.  seqlen_q must be 1 and causal is accepted and has no
- * effect for a single query token (the reference falls back to a kernel that
- * also assumes one query token).
+ * rather than rejected.  seqlen_q > 1 and causal are honoured as in
+ * fd_decode_paged_mq (the reference's fast paths reject them and its
+ * fallback kernel assumes one query token).
  */
 void run_kernel(const void* q, const void* k_cache_paged, const void* v_cache_paged, void* output,
                 const int32_t* cache_seqlens, const int32_t* block_table, int64_t batch_size,
@@ -89,6 +89,30 @@ int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, voi
                     int64_t num_heads_k, int64_t headdim, int64_t page_block_size,
                     int64_t num_blocks, int dtype, int out_dtype, float softmax_scale,
                     int64_t max_seqlen_k, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * fd_decode_paged_mq - fd_decode_paged for seqlen_q >= 1 query tokens per
+ * sequence (speculative / multi-token decode), with an optional causal mask.
+ * q and out are [B, seqlen_q, Hq, D]; lse (nullable) is [B, Hq, seqlen_q].
+ * The cached keys of sequence b are its cache_seqlens[b] tokens; with causal
+ * != 0 query token i sits at position cache_seqlens[b] - seqlen_q + i and
+ * sees keys up to that position (bottom-right alignment, as in
+ * flash_attn_with_kvcache); without it every query token sees all keys.
+ * Replaces: the seqlen_q and causal arguments of the reference run_kernel
+ * (best_flashattn_kvcache_decode.cu:1186-1201), which its fast paths reject
+ * (best :1235-1242) and its fallback ignores.
+ */
+int fd_decode_paged_mq(const void* q, const void* k_cache, const void* v_cache, void* out,
+                       float* lse, const int32_t* cache_seqlens, const int32_t* block_table,
+                       int64_t block_table_stride, int64_t batch_size, int64_t seqlen_q,
+                       int64_t num_heads, int64_t num_heads_k, int64_t headdim,
+                       int64_t page_block_size, int64_t num_blocks, int dtype, int out_dtype,
+                       float softmax_scale, int causal, int64_t max_seqlen_k, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* Workspace bytes fd_decode_paged_mq needs (same role as fd_decode_workspace_size). */
+size_t fd_decode_workspace_size_mq(int64_t batch_size, int64_t seqlen_q, int64_t num_heads,
+                                   int64_t num_heads_k, int64_t headdim);
 
 /*
  * fd_decode_paged_noalloc - fd_decode_paged for callers that cannot allocate

@@ -33,23 +33,26 @@ import torch
 def decode_reference(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                      cache_seqlens: torch.Tensor, block_table: torch.Tensor,
                      softmax_scale: float | None = None, rows=None,
-                     compute_dtype: torch.dtype = torch.float32):
+                     compute_dtype: torch.dtype = torch.float32, causal: bool = False):
     """Vectorised oracle (torch on CPU).
 
-    q [B, 1, Hq, D]; k_cache/v_cache [num_blocks, page, Hkv, D];
+    q [B, sq, Hq, D]; k_cache/v_cache [num_blocks, page, Hkv, D];
     cache_seqlens [B]; block_table [B, max_blocks].
-    Returns (out [B, 1, Hq, D], lse [B, Hq]) in compute_dtype; rows not in
-    `rows` (when given) are left zero / -inf.
+    Returns (out [B, sq, Hq, D], lse [B, Hq] for sq = 1 else [B, Hq, sq]) in
+    compute_dtype; rows not in `rows` (when given) are left zero / -inf.
+    causal: query token i sits at position L - sq + i and sees keys up to it
+    (the bottom-right convention of flash_attn_with_kvcache, which the
+    reference's run_kernel carries as its `causal` argument, best :1200).
     """
     q = q.cpu()
-    B, _, Hq, D = q.shape
+    B, sq, Hq, D = q.shape
     _, page, Hkv, _ = k_cache.shape
     G = Hq // Hkv
     scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
     seqlens = cache_seqlens.cpu().tolist()
     bt = block_table.cpu()
-    out = torch.zeros((B, 1, Hq, D), dtype=compute_dtype)
-    lse = torch.full((B, Hq), float("-inf"), dtype=compute_dtype)
+    out = torch.zeros((B, sq, Hq, D), dtype=compute_dtype)
+    lse = torch.full((B, Hq, sq), float("-inf"), dtype=compute_dtype)
     for b in (range(B) if rows is None else rows):
         L = max(0, int(seqlens[b]))
         if L == 0:
@@ -58,15 +61,19 @@ def decode_reference(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
         pages = bt[b, :n_pages].long()
         K = k_cache[pages.to(k_cache.device)].cpu().reshape(n_pages * page, Hkv, D)[:L].to(compute_dtype)
         V = v_cache[pages.to(v_cache.device)].cpu().reshape(n_pages * page, Hkv, D)[:L].to(compute_dtype)
-        qb = q[b, 0].to(compute_dtype).reshape(Hkv, G, D)
-        s = torch.einsum("hgd,lhd->hgl", qb, K) * scale
-        m = s.amax(dim=-1, keepdim=True)
-        e = torch.exp(s - m)
-        den = e.sum(dim=-1, keepdim=True)
-        o = torch.einsum("hgl,lhd->hgd", e / den, V)
-        out[b, 0] = o.reshape(Hq, D)
-        lse[b] = (m + torch.log(den)).reshape(Hq)
-    return out, lse
+        for i in range(sq):
+            vis = L - (sq - 1 - i) if causal else L
+            if vis <= 0:
+                continue
+            qb = q[b, i].to(compute_dtype).reshape(Hkv, G, D)
+            s = torch.einsum("hgd,lhd->hgl", qb, K[:vis]) * scale
+            m = s.amax(dim=-1, keepdim=True)
+            e = torch.exp(s - m)
+            den = e.sum(dim=-1, keepdim=True)
+            o = torch.einsum("hgl,lhd->hgd", e / den, V[:vis])
+            out[b, i] = o.reshape(Hq, D)
+            lse[b, :, i] = (m + torch.log(den)).reshape(Hq)
+    return out, (lse[:, :, 0] if sq == 1 else lse)
 
 
 def decode_reference_loops(q, k_cache, v_cache, cache_seqlens, block_table,

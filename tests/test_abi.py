@@ -58,10 +58,12 @@ def test_bad_arguments_return_status(lib, kw, code):
     assert status == code and msg
 
 
-def test_run_kernel_rejects_multi_token_queries_silently(lib):
+def test_run_kernel_rejects_bad_arguments_silently(lib):
     # Reference semantics: void return, nothing done; the reason is kept.
-    flashdecode.run_kernel(None, None, None, None, None, None, 1, 16, 2, 32, 8, 128, 16, 1, 0)
-    assert flashdecode.last_error()[0] == 2
+    flashdecode.run_kernel(None, None, None, None, None, None, 1, 16, 0, 32, 8, 128, 16, 1, 0)
+    assert flashdecode.last_error()[0] == 1  # seqlen_q must be >= 1
+    flashdecode.run_kernel(None, None, None, None, None, None, 1, 16, 2, 32, 8, 128, 16, 1, 1)
+    assert flashdecode.last_error()[0] == 1  # null tensors
     flashdecode.run_kernel(None, None, None, None, None, None, 4, 16, 1, 32, 8, 128, 16, 2, 0)
     assert flashdecode.last_error()[0] == 1  # num_blocks < batch: blocks_per_batch == 0
 

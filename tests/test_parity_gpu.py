@@ -222,3 +222,63 @@ def test_against_flash_attn_reference_oracle():
     err = (out.float() - ref.float()).abs()
     assert (err <= ATOL + RTOL * ref.float().abs()).all(), float(err.max())
     assert torch.allclose(lse, ref_lse.reshape(c.B, c.Hq).float(), atol=LSE_ATOL)
+
+
+MQ_LENGTHS = [1, 2, 3, 130, 1000, 257, 0]
+
+
+@pytest.mark.parametrize("sq,causal", [(2, True), (2, False), (3, True), (4, True)])
+@pytest.mark.parametrize("Hq,Hkv,page", [(32, 8, 256), (16, 8, 16), (8, 8, 64), (64, 8, 256)])
+def test_multi_token_queries(sq, causal, Hq, Hkv, page):
+    """seqlen_q > 1 with and without the bottom-right causal mask; rows of
+    query x group above 16 take the CUDA-core kernel."""
+    c = cases.custom_case(f"mq{sq}", torch.bfloat16, MQ_LENGTHS, Hq, Hkv, page=page, seed=sq)
+    t = cases.materialize(c, "cuda", seed=sq)
+    g = torch.Generator(device="cuda").manual_seed(sq)
+    q = torch.randn((c.B, sq, Hq, c.D), generator=g, device="cuda", dtype=torch.bfloat16)
+    out, lse = flashdecode.flash_decode(q, t["k_cache"], t["v_cache"], t["cache_seqlens"],
+                                        t["block_table"], return_softmax_lse=True, causal=causal)
+    ref_o, ref_l = decode_reference(q, t["k_cache"], t["v_cache"], t["cache_seqlens"],
+                                    t["block_table"], causal=causal)
+    err = (out.float().cpu() - ref_o).abs()
+    assert bool((err <= ATOL + RTOL * ref_o.abs()).all()), float(err.max())
+    fin = torch.isfinite(ref_l)
+    assert torch.equal(fin, torch.isfinite(lse.cpu()))
+    assert torch.allclose(lse.cpu()[fin], ref_l[fin], atol=LSE_ATOL)
+
+
+def test_reference_abi_multi_token_causal():
+    """run_kernel honours seqlen_q and causal (the reference's fast paths reject them)."""
+    c = cases.contest_case(16, 600, 8)
+    t = cases.materialize(c, "cuda", seed=0)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    q = torch.randn((c.B, 2, 32, 128), generator=g, device="cuda", dtype=torch.bfloat16)
+    out = torch.zeros_like(q)
+    flashdecode.run_kernel(q, t["k_cache"], t["v_cache"], out, t["cache_seqlens"], t["block_table"],
+                           c.B, 600, 2, 32, 8, 128, 16, c.num_blocks, 1)
+    torch.cuda.synchronize()
+    assert flashdecode.last_error()[0] == 0
+    ref_o, _ = decode_reference(q, t["k_cache"], t["v_cache"], t["cache_seqlens"], t["block_table"],
+                                causal=True)
+    err = (out.float().cpu() - ref_o).abs()
+    assert bool((err <= ATOL + RTOL * ref_o.abs()).all()), float(err.max())
+
+
+def test_multi_token_against_flash_attn():
+    fa = pytest.importorskip("flash_attn.flash_attn_interface")
+    c = cases.custom_case("mqfa", torch.bfloat16, [3000, 1200, 513, 4096], 32, 8, page=256, seed=3)
+    t = cases.materialize(c, "cuda", seed=3)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    q = torch.randn((c.B, 3, 32, 128), generator=g, device="cuda", dtype=torch.bfloat16)
+    try:
+        ref, ref_lse = fa.flash_attn_with_kvcache(q, t["k_cache"], t["v_cache"], None, None,
+                                                  cache_seqlens=t["cache_seqlens"],
+                                                  block_table=t["block_table"], causal=True,
+                                                  num_splits=0, return_softmax_lse=True)
+    except RuntimeError as e:
+        pytest.skip(f"flash_attn unavailable on this device: {e}")
+    out, lse = flashdecode.flash_decode(q, t["k_cache"], t["v_cache"], t["cache_seqlens"],
+                                        t["block_table"], return_softmax_lse=True, causal=True)
+    err = (out.float() - ref.float()).abs()
+    assert (err <= ATOL + RTOL * ref.float().abs()).all(), float(err.max())
+    assert torch.allclose(lse, ref_lse.float(), atol=LSE_ATOL)
