@@ -227,13 +227,14 @@ def main():
         total_kv = full.kv_bytes()
         t = cases.materialize(case, "cuda", seed=rank)
     else:
-        # config 4: every rank holds a page range of each sequence; partials
-        # are all-gathered over NCCL and merged
+        # config 4: every rank holds a page range of each sequence; the decode
+        # kernel pushes its partials to every rank over NVLink and a merge
+        # kernel on each rank combines them
         case, _page_map = fdist.kv_split_case(full, rank, world)
-        scaling, parallel = "strong", f"splitkv{world}"
+        scaling, parallel = "strong", f"splitkv{world}-p2p"
         total_kv = full.kv_bytes()
         t = cases.materialize(case, "cuda", seed=0)  # same q on every rank
-        splitter = fdist.SplitKVDecode(case.B, case.Hq, case.D, case.dtype, "cuda")
+        splitter = fdist.PeerSplitKVDecode(case.B, case.Hq, case.D, case.dtype, "cuda")
     max_len = max(int(case.seqlens.max()), 1)
 
     def decode(q, seqlens, bt):
@@ -310,6 +311,8 @@ def main():
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "us_per_call": round(e_ms * 1e3, 2),
                "steps": e_steps, "kv_cache": "resident in HBM (decode state, not a per-step input)"}
 
+    if splitter is not None:
+        splitter.close()
     if dist is not None:
         dist.destroy_process_group()
     if rank != 0:

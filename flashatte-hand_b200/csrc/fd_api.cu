@@ -226,13 +226,27 @@ size_t fd_decode_workspace_size(int64_t batch_size, int64_t num_heads, int64_t n
   return fd_decode_workspace_size_mq(batch_size, 1, num_heads, num_heads_k, headdim);
 }
 
-int fd_decode_paged_mq(const void* q, const void* k_cache, const void* v_cache, void* out,
-                       float* lse, const int32_t* cache_seqlens, const int32_t* block_table,
-                       int64_t block_table_stride, int64_t batch_size, int64_t seqlen_q,
-                       int64_t num_heads, int64_t num_heads_k, int64_t headdim,
-                       int64_t page_block_size, int64_t num_blocks, int dtype, int out_dtype,
-                       float softmax_scale, int causal, int64_t max_seqlen_k, void* workspace,
-                       size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Exchange-mode arguments of one cross-GPU split-KV step (see fd_xgpu.cu).
+struct ExchangeArgs {
+  int world;
+  float* part[fd::kMaxExchangeRanks];
+  uint32_t* flag[fd::kMaxExchangeRanks];
+  int64_t lse_off;
+  uint32_t epoch;
+};
+
+int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* out, float* lse,
+                const int32_t* cache_seqlens, const int32_t* block_table,
+                int64_t block_table_stride, int64_t batch_size, int64_t seqlen_q, int64_t num_heads,
+                int64_t num_heads_k, int64_t headdim, int64_t page_block_size, int64_t num_blocks,
+                int dtype, int out_dtype, float softmax_scale, int causal, int64_t max_seqlen_k,
+                void* workspace, size_t workspace_bytes, void* stream, const ExchangeArgs* xa,
+                int** err_word) {
+  if (xa != nullptr) out = xa->part[0];  // results go to the exchange parts
   if (q == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr ||
       cache_seqlens == nullptr || block_table == nullptr)
     return set_error(FD_ERR_INVALID_ARG, "null tensor pointer");
@@ -273,6 +287,10 @@ int fd_decode_paged_mq(const void* q, const void* k_cache, const void* v_cache, 
   const bool tensor_core_path = headdim == fd::kHeadDim && qrows <= fd::kMaxGroup && chunk > 0 &&
                                 aligned16(q) && aligned16(k_cache) && aligned16(v_cache) &&
                                 encode_fn() != nullptr;
+  if (xa != nullptr && (!tensor_core_path || batch_size > fd::kMaxBatchPerLaunch))
+    return set_error(FD_ERR_UNSUPPORTED,
+                     "cross-GPU exchange needs the tensor-core path and at most %d sequences",
+                     fd::kMaxBatchPerLaunch);
   if (!tensor_core_path) {
     fd::SimtParams sp;
     sp.q = q; sp.k = k_cache; sp.v = v_cache; sp.out = out; sp.lse = lse;
@@ -371,11 +389,138 @@ int fd_decode_paged_mq(const void* q, const void* k_cache, const void* v_cache, 
     p.epoch = next_epoch();
     p.cost_tile = cost_tile();
     p.cost_seg = cost_seg();
+    p.xworld = 0;
+    if (xa != nullptr) {
+      p.xworld = xa->world;
+      for (int j = 0; j < fd::kMaxExchangeRanks; ++j) {
+        p.xpart[j] = j < xa->world ? xa->part[j] : nullptr;
+        p.xflag[j] = j < xa->world ? xa->flag[j] : nullptr;
+      }
+      p.xlse_off = xa->lse_off;
+      p.xepoch = xa->epoch;
+      p.xdone = reinterpret_cast<uint32_t*>(ws + wl.done_off);
+      const cudaError_t ez = cudaMemsetAsync(p.xdone, 0, sizeof(uint32_t), st);
+      if (ez != cudaSuccess) return set_error(FD_ERR_CUDA, "clear done counter: %s", cudaGetErrorString(ez));
+    }
+    if (err_word != nullptr) *err_word = p.err;
     const int64_t work_bound = nb * num_heads_k * tiles_bound;
     const int grid = static_cast<int>(work_bound < sms ? work_bound : sms);
     const cudaError_t e = fd::launch_decode_sm100(maps, p, dtype, out_fp32, grid, st);
     if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "sm100 launch: %s", cudaGetErrorString(e));
   }
+  return set_ok();
+}
+
+}  // namespace
+
+extern "C" {
+
+int fd_decode_paged_mq(const void* q, const void* k_cache, const void* v_cache, void* out,
+                       float* lse, const int32_t* cache_seqlens, const int32_t* block_table,
+                       int64_t block_table_stride, int64_t batch_size, int64_t seqlen_q,
+                       int64_t num_heads, int64_t num_heads_k, int64_t headdim,
+                       int64_t page_block_size, int64_t num_blocks, int dtype, int out_dtype,
+                       float softmax_scale, int causal, int64_t max_seqlen_k, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  return decode_impl(q, k_cache, v_cache, out, lse, cache_seqlens, block_table, block_table_stride,
+                     batch_size, seqlen_q, num_heads, num_heads_k, headdim, page_block_size,
+                     num_blocks, dtype, out_dtype, softmax_scale, causal, max_seqlen_k, workspace,
+                     workspace_bytes, stream, nullptr, nullptr);
+}
+
+size_t fd_xgpu_buffer_size(int64_t batch_size, int64_t seqlen_q, int64_t num_heads, int world) {
+  if (batch_size <= 0 || seqlen_q <= 0 || num_heads <= 0 || world <= 0 ||
+      world > fd::kMaxExchangeRanks)
+    return 0;
+  const int64_t rows = batch_size * seqlen_q * num_heads;
+  const int64_t part = ((rows * (fd::kHeadDim + 1) + 63) / 64) * 64;  // floats, 256 B aligned
+  return 2 * 256 + 2 * static_cast<size_t>(world) * part * sizeof(float);
+}
+
+int fd_xgpu_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  if (ptr == nullptr || ipc_handle == nullptr || bytes == 0)
+    return set_error(FD_ERR_INVALID_ARG, "null pointer or zero size");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    if (p != nullptr) cudaFree(p);
+    return set_error(FD_ERR_CUDA, "exchange buffer: %s", cudaGetErrorString(e));
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  return set_ok();
+}
+
+int fd_xgpu_open(const void* ipc_handle, void** ptr) {
+  if (ptr == nullptr || ipc_handle == nullptr) return set_error(FD_ERR_INVALID_ARG, "null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "open peer buffer: %s", cudaGetErrorString(e));
+  return set_ok();
+}
+
+int fd_xgpu_close(void* ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "close peer buffer: %s", cudaGetErrorString(e));
+  return set_ok();
+}
+
+int fd_xgpu_free(void* ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "free exchange buffer: %s", cudaGetErrorString(e));
+  return set_ok();
+}
+
+int fd_decode_paged_xgpu(const void* q, const void* k_cache, const void* v_cache,
+                         const int32_t* cache_seqlens, const int32_t* block_table,
+                         int64_t block_table_stride, int64_t batch_size, int64_t seqlen_q,
+                         int64_t num_heads, int64_t num_heads_k, int64_t headdim,
+                         int64_t page_block_size, int64_t num_blocks, int dtype, int out_dtype,
+                         float softmax_scale, int causal, int64_t max_seqlen_k, int rank,
+                         int world, void* const* xbufs, uint64_t step, void* out, float* lse,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (xbufs == nullptr || out == nullptr) return set_error(FD_ERR_INVALID_ARG, "null pointer");
+  if (world < 1 || world > fd::kMaxExchangeRanks || rank < 0 || rank >= world)
+    return set_error(FD_ERR_INVALID_ARG, "rank %d / world %d", rank, world);
+  if (batch_size <= 0 || seqlen_q <= 0 || num_heads <= 0)
+    return set_error(FD_ERR_INVALID_ARG, "sizes must be positive");
+  if (out_dtype != dtype && out_dtype != FD_DTYPE_FP32)
+    return set_error(FD_ERR_INVALID_ARG, "out_dtype must equal dtype or be fp32");
+  for (int j = 0; j < world; ++j)
+    if (xbufs[j] == nullptr) return set_error(FD_ERR_INVALID_ARG, "exchange buffer %d is null", j);
+  const int64_t rows = batch_size * seqlen_q * num_heads;
+  const int64_t part = ((rows * (fd::kHeadDim + 1) + 63) / 64) * 64;
+  const int half = static_cast<int>(step & 1);
+  // Buffer: [flags half 0 | flags half 1 | parts half 0 | parts half 1],
+  // flags 256 B per half (one u32 per rank), parts world * `part` floats.
+  ExchangeArgs xa;
+  xa.world = world;
+  xa.lse_off = rows * fd::kHeadDim;
+  xa.epoch = static_cast<uint32_t>(step % 0x7FFFFFFFull) + 1u;
+  for (int j = 0; j < world; ++j) {
+    uint8_t* base = static_cast<uint8_t*>(xbufs[j]);
+    xa.flag[j] = reinterpret_cast<uint32_t*>(base + half * 256) + rank;
+    xa.part[j] = reinterpret_cast<float*>(base + 512) + (static_cast<int64_t>(half) * world + rank) * part;
+  }
+  int* err = nullptr;
+  const int st = decode_impl(q, k_cache, v_cache, nullptr, nullptr, cache_seqlens, block_table,
+                             block_table_stride, batch_size, seqlen_q, num_heads, num_heads_k,
+                             headdim, page_block_size, num_blocks, dtype, FD_DTYPE_FP32,
+                             softmax_scale, causal, max_seqlen_k, workspace, workspace_bytes,
+                             stream, &xa, &err);
+  if (st != FD_OK) return st;
+  uint8_t* mine = static_cast<uint8_t*>(xbufs[rank]);
+  const float* parts = reinterpret_cast<const float*>(mine + 512) + static_cast<int64_t>(half) * world * part;
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(mine + half * 256);
+  const cudaError_t e = fd::launch_exchange_combine(
+      parts, part, rows * fd::kHeadDim, flags, world, xa.epoch, rows, static_cast<int>(seqlen_q),
+      static_cast<int>(num_heads), out, out_dtype, lse, err, timeout_ns(),
+      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "exchange combine: %s", cudaGetErrorString(e));
   return set_ok();
 }
 

@@ -586,7 +586,8 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     };
     // Segment epilogue: direct output, or partial + (last arrival) merge.
     int fin_buf = 0;
-    auto finish = [&](const Segment& sg, const State& st) {
+    // `scratch`: a P buffer no P.V is reading (used when merging a split pair).
+    auto finish = [&](const Segment& sg, const State& st, uint8_t* scratch) {
       float* fb = fin + fin_buf * (4 * kMaxGroup);
       fin_buf ^= 1;
 #pragma unroll
@@ -611,15 +612,31 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         const int qi = MULTI ? h / group : 0, g = h - qi * group;
         return (static_cast<int64_t>(sg.b) * hq + sg.kvh * group + g) * sq + qi;
       };
+      // Result writers: the output (and LSE), or, in a cross-GPU exchange,
+      // this rank's part in every rank's exchange buffer.
+      auto put_o = [&](int64_t oi, float v) {
+        if (p.xworld > 0) {
+          for (int j = 0; j < p.xworld; ++j) p.xpart[j][oi] = v;
+        } else {
+          out[oi] = to_out<OutT>(v);
+        }
+      };
+      auto put_lse = [&](int64_t li, float v) {
+        if (p.xworld > 0) {
+          for (int j = 0; j < p.xworld; ++j) p.xpart[j][p.xlse_off + li] = v;
+        } else if (p.lse != nullptr) {
+          p.lse[li] = v;
+        }
+      };
       if (sg.nseg == 1) {
 #pragma unroll
         for (int h = 0; h < NCOL; ++h) {
           if (h < qrows) {
             const float v = l_tot[h] > 0.f ? st.o[h] / l_tot[h] : 0.f;
-            out[out_index(h)] = to_out<OutT>(v);
-            if (p.lse != nullptr && d == h)
-              p.lse[lse_index(h)] =
-                  l_tot[h] > 0.f ? (st.m[h] + fast_log2(l_tot[h])) * 0.69314718055994531f : neg_inf;
+            put_o(out_index(h), v);
+            if (d == h)
+              put_lse(lse_index(h),
+                      l_tot[h] > 0.f ? (st.m[h] + fast_log2(l_tot[h])) * 0.69314718055994531f : neg_inf);
           }
         }
         return;
@@ -646,21 +663,32 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       if (!merge) return;
       __threadfence();
       const int64_t sbase = static_cast<int64_t>(sg.cfirst) + sg.pair;
+      // The pair's nseg x qrows partial LSEs are contiguous: stage them in a
+      // free P buffer with one parallel load, so the per-head weights come
+      // from shared memory and only the independent partial-O loads remain.
+      const int nl = sg.nseg * qrows;
+      float* sl = reinterpret_cast<float*>(scratch);
+      const bool staged = nl <= kPBufBytes / 4;
+      if (staged) {
+        for (int i = d; i < nl; i += 128) sl[i] = __ldcg(p.part_lse + sbase * qrows + i);
+        named_bar_sync(1, 128);
+      }
       for (int h = 0; h < qrows; ++h) {
+        auto lse_of = [&](int j) {
+          return staged ? sl[j * qrows + h] : __ldcg(p.part_lse + (sbase + j) * qrows + h);
+        };
         float mx = neg_inf;
-        for (int j = 0; j < sg.nseg; ++j) mx = fmaxf(mx, __ldcg(p.part_lse + (sbase + j) * qrows + h));
+        for (int j = 0; j < sg.nseg; ++j) mx = fmaxf(mx, lse_of(j));
         float den = 0.f, acc = 0.f;
+#pragma unroll 4
         for (int j = 0; j < sg.nseg; ++j) {
-          const float lj = __ldcg(p.part_lse + (sbase + j) * qrows + h);
-          const float wj = lj == neg_inf ? 0.f : fast_exp2(lj - mx);
-          if (wj > 0.f) {
-            acc = fmaf(wj, __ldcg(p.part_o + ((sbase + j) * qrows + h) * kHeadDim + d), acc);
-            den += wj;
-          }
+          const float lj = lse_of(j);
+          const float wj = lj == neg_inf ? 0.f : fast_exp2(lj - mx);  // empty parts hold O = 0
+          acc = fmaf(wj, __ldcg(p.part_o + ((sbase + j) * qrows + h) * kHeadDim + d), acc);
+          den += wj;
         }
-        out[out_index(h)] = to_out<OutT>(den > 0.f ? acc / den : 0.f);
-        if (p.lse != nullptr && d == 0)
-          p.lse[lse_index(h)] = den > 0.f ? (mx + fast_log2(den)) * 0.69314718055994531f : neg_inf;
+        put_o(out_index(h), den > 0.f ? acc / den : 0.f);
+        if (d == 0) put_lse(lse_index(h), den > 0.f ? (mx + fast_log2(den)) * 0.69314718055994531f : neg_inf);
       }
     };
 
@@ -760,7 +788,8 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         if (prev_open) {
 #pragma unroll
           for (int h = 0; h < NCOL; ++h) prev.o[h] = fmaf(prev.o[h], prev.a[h], ov[h]);
-          finish(prev_seg, prev);
+          // P.V(it-1) is done, so its P buffer is free until tile it+1's softmax
+          finish(prev_seg, prev, pbufs + ((it + 1) & 1) * kPBufBytes);
         } else {
 #pragma unroll
           for (int h = 0; h < NCOL; ++h) cur.o[h] = fmaf(cur.o[h], cur.a[h], ov[h]);
@@ -774,13 +803,24 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       load_o(it - 1, ov);
 #pragma unroll
       for (int h = 0; h < NCOL; ++h) cur.o[h] = fmaf(cur.o[h], cur.a[h], ov[h]);
-      finish(seg, cur);
+      finish(seg, cur, pbufs);  // every P.V is done
     }
   }
 
   // ------------------------------------------------------------ teardown
   tc_fence_before();
   __syncthreads();
+  if (p.xworld > 0 && tid == 0 && !*abort_flag) {
+    // After the CTA barrier, one system-scope fence publishes the CTA's
+    // exchange writes; the CTA that finishes last on this GPU then tells
+    // every rank that this rank's part is complete (the host zeroes xdone
+    // before each launch).
+    __threadfence_system();
+    if (atomicAdd(p.xdone, 1u) == gridDim.x - 1u) {
+      __threadfence_system();
+      for (int j = 0; j < p.xworld; ++j) st_release_sys_u32(p.xflag[j], p.xepoch);
+    }
+  }
   if (*abort_flag) {
     if (tid == 0) {
       atomicExch(p.err, 5);
@@ -837,6 +877,7 @@ WorkspaceLayout workspace_layout(int64_t batch_per_launch, int64_t num_heads_k, 
   const size_t slots = pairs + static_cast<size_t>(grid_max);
   WorkspaceLayout w;
   w.err_off = 0;
+  w.done_off = 128;
   w.tickets_off = 256;
   w.lse_off = w.tickets_off + up(pairs * 4);
   w.o_off = w.lse_off + up(slots * qrows * 4);

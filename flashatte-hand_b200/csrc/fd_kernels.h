@@ -12,6 +12,7 @@ constexpr int kHeadDim = 128;          // head dim of the tensor-core path
 constexpr int kTileTokens = 128;       // KV tokens per pipeline stage (UMMA M of Q.K^T)
 constexpr int kMaxGroup = 16;          // query heads per KV head (UMMA N, padded)
 constexpr int kMaxBatchPerLaunch = 512;   // sequences per launch (schedule lives in smem)
+constexpr int kMaxExchangeRanks = 8;   // GPUs of one node in a cross-GPU split-KV exchange
 constexpr int kSm100Threads = 224;     // warps 0/6 TMA, warp 1 MMA, warps 2-5 softmax/epilogue
 
 // Per-launch parameters of the tensor-core kernel (tensor maps travel as
@@ -32,6 +33,16 @@ struct DecodeParams {
   int* err;                   // device error word
   unsigned long long timeout_ns;
   uint32_t epoch;             // 1 .. 2^20-1, different for consecutive launches
+  // Cross-GPU split-KV exchange (xworld > 0): instead of out/lse, every
+  // result row goes as fp32 O and ln-LSE to each rank's exchange part
+  // xpart[j] (O at [row*128 + d], LSE at [xlse_off + lse row]); the CTA that
+  // finishes last on this GPU then stores xepoch to each rank's flag xflag[j].
+  int xworld;
+  float* xpart[kMaxExchangeRanks];
+  uint32_t* xflag[kMaxExchangeRanks];
+  int64_t xlse_off;
+  uint32_t xepoch;
+  uint32_t* xdone;            // count of finished CTAs (workspace, zeroed before the launch)
   int cost_tile, cost_seg;    // split cost model: fixed cost per tile and per pair, in
                               // units where a full tile's K/V bytes cost 8
 };
@@ -49,7 +60,7 @@ struct SimtParams {
 
 // Workspace carve-up for the tensor-core kernel.
 struct WorkspaceLayout {
-  size_t err_off, tickets_off, lse_off, o_off, total;
+  size_t err_off, done_off, tickets_off, lse_off, o_off, total;
 };
 WorkspaceLayout workspace_layout(int64_t batch_per_launch, int64_t num_heads_k, int64_t qrows,
                                  int grid_max);
@@ -68,6 +79,14 @@ cudaError_t launch_decode_simt(const SimtParams& p, int dtype, bool out_fp32, cu
 cudaError_t launch_combine_lse(const float* part_o, int64_t o_stride, const float* part_lse,
                                int64_t l_stride, int64_t n_parts, int64_t rows, int64_t head_dim,
                                void* out, int out_dtype, float* lse_out, cudaStream_t stream);
+
+// Cross-GPU split-KV exchange: merge the `world` parts of this rank's
+// exchange buffer half once every rank's flag in it reads `epoch` (bounded
+// wait; on expiry *err = FD_ERR_DEVICE_TIMEOUT and nothing is written).
+cudaError_t launch_exchange_combine(const float* parts, int64_t part_stride, int64_t lse_off,
+                                    const uint32_t* flags, int world, uint32_t epoch, int64_t rows,
+                                    int sq, int hq, void* out, int out_dtype, float* lse_out,
+                                    int* err, unsigned long long timeout_ns, cudaStream_t stream);
 
 cudaError_t launch_bounded_wait_probe(unsigned long long budget_ns, int* status,
                                       unsigned long long* waited_ns, cudaStream_t stream);

@@ -28,6 +28,14 @@ SIGNATURES: dict[str, tuple] = {
                                 + [_i32, _i32, _f32, _i64, _vp]),
     "fd_decode_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
     "fd_combine_lse": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _vp, _vp]),
+    "fd_xgpu_buffer_size": (_sz, [_i64, _i64, _i64, _i32]),
+    "fd_xgpu_alloc": (_i32, [_sz, _c.POINTER(_vp), _c.c_char_p]),
+    "fd_xgpu_open": (_i32, [_c.c_char_p, _c.POINTER(_vp)]),
+    "fd_xgpu_close": (_i32, [_vp]),
+    "fd_xgpu_free": (_i32, [_vp]),
+    "fd_decode_paged_xgpu": (_i32, [_vp, _vp, _vp, _vp, _vp] + [_i64] * 8
+                             + [_i32, _i32, _f32, _i32, _i64, _i32, _i32, _c.POINTER(_vp),
+                                _c.c_uint64, _vp, _vp, _vp, _sz, _vp]),
     "fd_last_error": (_i32, []),
     "fd_error_string": (_c.c_char_p, [_i32]),
     "fd_last_error_message": (_c.c_char_p, []),

@@ -7,21 +7,28 @@ partitions are provided here:
 * batch sharding (``batch_shard``): each rank owns whole sequences and their
   KV pages, chosen longest-first (LPT) so skewed length mixes balance.  No
   collective is on the data path; every rank writes its own output rows.
-* cross-GPU split-KV (``kv_split_case`` + ``SplitKVDecode``): each rank owns
-  a contiguous page range of every sequence, decodes it to a normalised fp32
-  partial (O, LSE), and one all-gather of the packed [O | LSE] blocks
-  (B*Hq*(D+1) floats per rank) feeds the LSE combine kernel, which reads the
-  gathered buffer from local memory.  That is the reference's split/combine
-  (best :595-1037) with the splits placed on different GPUs.
+* cross-GPU split-KV (``kv_split_case``): each rank owns a contiguous page
+  range of every sequence and decodes it to a normalised fp32 partial
+  (O, LSE) per output row; the ranks' partials are merged with LSE weights.
+  That is the reference's split/combine (best :595-1037) with the splits
+  placed on different GPUs.  ``PeerSplitKVDecode`` is the product path: the
+  decode kernel itself stores its partial into every rank's exchange buffer
+  over NVLink (peer mappings of buffers swapped as IPC handles) and a merge
+  kernel on each rank waits for all ranks' flags.  ``SplitKVDecode`` runs the
+  same protocol through a collective (all-gather of packed [O | LSE] blocks,
+  B*Hq*(D+1) floats per rank) with injectable decode/merge steps; the CPU
+  tests drive it over gloo.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
 import torch.distributed as tdist
 
 from . import cases as _cases
+from ._lib import FD_DTYPE_BF16, FD_DTYPE_FP16, FD_DTYPE_FP32, check, load_library
 
 
 def batch_shard(case: _cases.DecodeCase, rank: int, world: int):
@@ -111,3 +118,87 @@ class SplitKVDecode:
         part_l = parts[:, self.rows * self.D:]
         out, lse = self.combine_fn(part_o, part_l, self.out_dtype)
         return out.view(self.B, 1, self.Hq, self.D), lse.view(self.B, self.Hq)
+
+
+_DT = {torch.bfloat16: FD_DTYPE_BF16, torch.float16: FD_DTYPE_FP16, torch.float32: FD_DTYPE_FP32}
+
+
+class PeerSplitKVDecode:
+    """Cross-GPU split-KV decode step over peer memory (one process per GPU).
+
+    Set-up (collective, every rank): allocate this rank's exchange buffer,
+    swap IPC handles over the process group, map the peers' buffers.  Each
+    call then launches two kernels on the current stream: the decode kernel,
+    which writes this rank's partial for every output row into every rank's
+    buffer and flags it, and the merge kernel, which waits for all ranks'
+    flags and writes the full result on every rank.  Every rank must make the
+    same sequence of calls.
+    """
+
+    def __init__(self, B: int, Hq: int, D: int, out_dtype: torch.dtype, device, group=None,
+                 seqlen_q: int = 1):
+        self.lib = load_library()
+        self.B, self.Hq, self.D, self.sq = B, Hq, D, seqlen_q
+        self.out_dtype = out_dtype
+        self.device = torch.device(device)
+        self.group = group
+        self.world = tdist.get_world_size(group)
+        self.rank = tdist.get_rank(group)
+        size = self.lib.fd_xgpu_buffer_size(B, seqlen_q, Hq, self.world)
+        if size == 0:
+            raise ValueError("unsupported exchange shape")
+        own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        with torch.cuda.device(self.device):
+            check(self.lib.fd_xgpu_alloc(size, ctypes.byref(own), handle))
+        self._own = own.value
+        handles = [None] * self.world
+        tdist.all_gather_object(handles, handle.raw, group=group)
+        ptrs, self._opened = [], []
+        with torch.cuda.device(self.device):
+            for j, h in enumerate(handles):
+                if j == self.rank:
+                    ptrs.append(self._own)
+                    continue
+                p = ctypes.c_void_p()
+                check(self.lib.fd_xgpu_open(h, ctypes.byref(p)))
+                ptrs.append(p.value)
+                self._opened.append(p.value)
+        self.xbufs = (ctypes.c_void_p * self.world)(*ptrs)
+        self.step = 0
+        tdist.barrier(group=group)
+
+    def __call__(self, q, k_local, v_local, seqlens_local, bt_local, softmax_scale: float,
+                 causal: bool = False, out=None, lse=None):
+        B, sq, Hq, D = q.shape
+        if out is None:
+            out = torch.empty((B, sq, Hq, D), dtype=self.out_dtype, device=q.device)
+        if lse is None:
+            lse = torch.empty((B, Hq) if sq == 1 else (B, Hq, sq), dtype=torch.float32,
+                              device=q.device)
+        st = torch.cuda.current_stream(q.device)
+        nb, page, Hkv, _ = k_local.shape
+        with torch.cuda.device(q.device):
+            status = self.lib.fd_decode_paged_xgpu(
+                q.data_ptr(), k_local.data_ptr(), v_local.data_ptr(), seqlens_local.data_ptr(),
+                bt_local.data_ptr(), bt_local.shape[1], B, sq, Hq, Hkv, D, page, nb, _DT[q.dtype],
+                _DT[self.out_dtype], float(softmax_scale), 1 if causal else 0, 0, self.rank,
+                self.world, self.xbufs, self.step, out.data_ptr(), lse.data_ptr(), None, 0,
+                st.cuda_stream)
+        check(status)
+        self.step += 1
+        return out, lse
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (collective)."""
+        torch.cuda.synchronize(self.device)
+        tdist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                check(self.lib.fd_xgpu_close(p))
+            self._opened = []
+        tdist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            if self._own:
+                check(self.lib.fd_xgpu_free(self._own))
+                self._own = None

@@ -166,6 +166,40 @@ int fd_combine_lse(const float* part_o, int64_t part_o_stride, const float* part
                    int64_t part_lse_stride, int64_t n_parts, int64_t rows, int64_t headdim,
                    void* out, int out_dtype, float* lse_out, void* stream);
 
+/*
+ * Cross-GPU split-KV decode over peer memory (one process per GPU of a node).
+ *
+ * Each rank holds a page range of every sequence (its own cache_seqlens and
+ * block_table describe that range) and an exchange buffer of
+ * fd_xgpu_buffer_size() bytes made by fd_xgpu_alloc; the ranks swap the
+ * 64-byte IPC handles (any host channel) and map each other's buffers with
+ * fd_xgpu_open.  fd_decode_paged_xgpu then runs one step: the decode kernel
+ * writes this rank's partial (O, LSE) for every output row straight into
+ * every rank's buffer over NVLink and flags it; a merge kernel waits (bounded,
+ * FD_ERR_DEVICE_TIMEOUT in the workspace error word on expiry) for all ranks'
+ * flags and writes out [B, sq, Hq, D] and lse [B, Hq, sq] on every rank.
+ * xbufs: host array of `world` device pointers, entry rank = own buffer.
+ * step: call counter, the same on every rank, +1 per call (the buffer is
+ * double-buffered by its parity).  Needs the tensor-core path (head dim 128,
+ * seqlen_q * Hq / Hkv <= 16) and batch_size <= 512.
+ * Replaces: the reference's split combine (best_flashattn_kvcache_decode.cu
+ * :956-1037, :1420-1425) with the splits on different GPUs; the reference has
+ * no multi-GPU code.
+ */
+size_t fd_xgpu_buffer_size(int64_t batch_size, int64_t seqlen_q, int64_t num_heads, int world);
+int fd_xgpu_alloc(size_t bytes, void** ptr, void* ipc_handle);
+int fd_xgpu_open(const void* ipc_handle, void** ptr);
+int fd_xgpu_close(void* ptr);
+int fd_xgpu_free(void* ptr);
+int fd_decode_paged_xgpu(const void* q, const void* k_cache, const void* v_cache,
+                         const int32_t* cache_seqlens, const int32_t* block_table,
+                         int64_t block_table_stride, int64_t batch_size, int64_t seqlen_q,
+                         int64_t num_heads, int64_t num_heads_k, int64_t headdim,
+                         int64_t page_block_size, int64_t num_blocks, int dtype, int out_dtype,
+                         float softmax_scale, int causal, int64_t max_seqlen_k, int rank,
+                         int world, void* const* xbufs, uint64_t step, void* out, float* lse,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
 /* Status of the last call made on this host thread, and its message. */
 int fd_last_error(void);
 const char* fd_error_string(int code);

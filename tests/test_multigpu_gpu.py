@@ -44,7 +44,23 @@ def _worker(rank, port, kind, q):
         t = cases.materialize(glob, "cuda", seed=5)  # identical on every rank
         ref_o, ref_l = flashdecode.flash_decode(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"],
                                                 t["block_table"], return_softmax_lse=True)
-        if kind == "splitkv":
+        if kind == "peer":
+            local, page_map = fdist.kv_split_case(glob, rank, WORLD)
+            pm = page_map.to("cuda")
+            k, v = t["k_cache"][pm].contiguous(), t["v_cache"][pm].contiguous()
+            step = fdist.PeerSplitKVDecode(glob.B, glob.Hq, glob.D, torch.bfloat16, "cuda")
+            for _ in range(5):  # both buffer halves, several epochs
+                out, lse = step(t["q"], k, v, local.seqlens.cuda(), local.block_table.cuda(),
+                                glob.softmax_scale)
+            torch.cuda.synchronize()
+            assert flashdecode.device_status() == 0
+            err = (out.float() - ref_o.float()).abs()
+            assert bool((err <= 2e-3 + 1e-2 * ref_o.float().abs()).all()), float(err.max())
+            fin = torch.isfinite(ref_l)
+            assert torch.equal(fin, torch.isfinite(lse))
+            assert torch.allclose(lse[fin], ref_l[fin], atol=1e-3)
+            step.close()
+        elif kind == "splitkv":
             local, page_map = fdist.kv_split_case(glob, rank, WORLD)
             pm = page_map.to("cuda")
             k, v = t["k_cache"][pm].contiguous(), t["v_cache"][pm].contiguous()
@@ -100,6 +116,10 @@ def _run(kind):
 
 def test_split_kv_across_two_gpus():
     _run("splitkv")
+
+
+def test_split_kv_over_peer_memory_two_gpus():
+    _run("peer")
 
 
 def test_batch_shard_across_two_gpus():
