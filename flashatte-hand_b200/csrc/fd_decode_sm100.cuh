@@ -1,0 +1,885 @@
+// fd_decode_sm100.cuh - persistent split-KV paged decode kernel for B200
+// (device code and launch templates; fd_decode_sm100_*.cu instantiate it).
+//
+// Work decomposition (replaces the reference's fixed split table and
+// per-split grid, submission-oj/best_flashattn_kvcache_decode.cu:1039-1076,
+// :1381-1418, and its balanced page ranges :664-671): every (sequence b,
+// KV head) pair is a row of 128-token tiles; the rows are laid end to end
+// (b-major, then KV head) and the line is cut into contiguous ranges of
+// equal estimated cost (K/V bytes of each tile + a fixed cost per tile + a
+// fixed cost per pair), one per persistent CTA.  A CTA walks its range
+// segment by segment (a segment = the part of one pair inside the range).
+// A pair that lies inside one CTA is written straight to the output; a pair
+// cut by range boundaries leaves one normalised partial (O, log2-LSE) per
+// segment and the CTA that finishes last merges them (replaces the separate
+// combine launch, best :956-1037, :1420-1425).
+//
+// Per tile the CTA runs, warp-specialised:
+//   warps 0,6 TMA producers: gather the tile's K (warp 0, with the group's
+//             query rows) and V (warp 6) rows page by page through
+//             block_table into a 3-deep shared-memory ring (128B-swizzled,
+//             two 64-dim halves); a sequence's last, partial tile is fetched
+//             in 16-token boxes covering only its valid rows.
+//   warp 1    tcgen05 issuer: S^T[tok, head] = K . Q^T (M=128 tokens, N=16
+//             heads, K=128 dims) into TMEM, then O^T[dim, head] = V^T . P^T
+//             (M=128 dims, N=2x16 heads, K=128 tokens) into TMEM, each issued
+//             as soon as its inputs are ready (no fixed QK/PV interleave).
+//   warps 2-5 softmax + epilogue: thread = TMEM lane = token row for S and
+//             head-dim for O; fp32 online softmax in the log2 domain (the
+//             reference's convention, best :541-578), P written to shared
+//             memory for the second UMMA, per-tile O folded into registers.
+// One KV byte is read from HBM exactly once; the arithmetic runs on the
+// tensor cores so the SM's issue slots stay free for the memory pipeline.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <type_traits>
+
+#include "fd_kernels.h"
+#include "fd_ptx.cuh"
+
+namespace fd {
+
+namespace {
+
+constexpr int kStages = 3;
+constexpr int kHalfBytes = kTileTokens * 128;    // 128 tokens x 64 dims x 2 B = 16 KB
+constexpr int kOperandBytes = 2 * kHalfBytes;    // one K or V tile: 32 KB
+constexpr int kQSlotBytes = 2 * kMaxGroup * 128; // two halves x 16 rows x 128 B
+constexpr int kStageBytes = 2 * kOperandBytes + kQSlotBytes;  // K + V + Q: 68 KB
+// P is stored as two 16-bit parts, P = hi + lo (hi = round(P), lo = round(P - hi)),
+// side by side in the UMMA N dimension: 128 tokens x (2 x 16 heads) x 2 B.
+// Summing V.hi and V.lo keeps P's fp32 precision through a 16-bit MMA.
+constexpr int kPBufBytes = kTileTokens * 2 * kMaxGroup * 2;
+constexpr int kTmemCols = 128;                   // S0 S1 (16 cols each), O0 O1 (32 each)
+constexpr int kNumBars = 2 * kStages + 10;
+constexpr int kVProducerWarp = 6;
+
+// Shared-memory carve-up, offsets from a 1024-byte aligned base.
+constexpr int kOffStages = 0;
+constexpr int kOffP = kOffStages + kStages * kStageBytes;
+constexpr int kOffBars = kOffP + 2 * kPBufBytes;
+constexpr int kOffMisc = kOffBars + kNumBars * 8;            // tmem slot, abort, last flag
+constexpr int kOffRed = (kOffMisc + 64 + 15) & ~15;          // [2][4][16] floats tile maxima
+constexpr int kOffFin = kOffRed + 2 * 4 * kMaxGroup * 4;     // [2][4][16] floats row sums
+constexpr int kOffPrefix = kOffFin + 2 * 4 * kMaxGroup * 4;  // [B+1] ints pair-cost prefix sums
+constexpr int kOffLens = kOffPrefix + (kMaxBatchPerLaunch + 1) * 4;  // [B] ints clamped lengths
+constexpr int kSmemUsed = kOffLens + kMaxBatchPerLaunch * 4;
+constexpr int kSmemBytes = kSmemUsed + 1024;                 // slack for 1024-B alignment
+static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
+
+// TMEM columns: S^T of tile parity b at 16*b, O^T of tile parity b at 32+32*b.
+__device__ __forceinline__ uint32_t col_s(int b) { return static_cast<uint32_t>(b) * 16u; }
+__device__ __forceinline__ uint32_t col_o(int b) { return 32u + static_cast<uint32_t>(b) * 32u; }
+
+// Arrival counter of a split (sequence, KV head) pair: bits [12, 32) hold the
+// launch epoch, bits [0, 12) the arrivals seen in that epoch.  A counter left
+// by any earlier launch (even one that stopped early) reads as zero, so the
+// workspace never needs clearing.  Returns true for the pair's last arrival.
+__device__ __forceinline__ bool ticket_arrive(uint32_t* t, uint32_t epoch, int nseg) {
+  uint32_t old = atomicAdd(t, 0u);
+  for (;;) {
+    const uint32_t cnt = (old >> 12) == epoch ? (old & 0xFFFu) : 0u;
+    const uint32_t nv = (epoch << 12) | (cnt + 1u);
+    const uint32_t prev = atomicCAS(t, old, nv);
+    if (prev == old) return cnt + 1u == static_cast<uint32_t>(nseg);
+    old = prev;
+  }
+}
+
+// UMMA shared-memory descriptor (tcgen05 matrix descriptor): start address,
+// leading/stride byte offsets (16-byte units), version 1, layout type.
+__device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                               uint32_t layout) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;
+  d |= static_cast<uint64_t>(layout) << 61;
+  return d;
+}
+constexpr uint32_t kLayoutNone = 0;
+constexpr uint32_t kLayoutSw128 = 2;
+
+// UMMA instruction descriptor for kind::f16 with an fp32 accumulator.
+__host__ __device__ constexpr uint32_t make_idesc(bool bf16, bool a_mn_major, bool b_mn_major,
+                                                  int m, int n) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
+         ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// split2(a, b): hi = round-to-nearest 16-bit pair of (a, b), lo = the same
+// rounding of the residuals (a - hi.x, b - hi.y); hi + lo carries ~16 more
+// mantissa bits than hi alone.
+template <typename T> struct DType;
+template <> struct DType<__nv_bfloat16> {
+  static constexpr bool kBf16 = true;
+  static __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+  }
+};
+template <> struct DType<__half> {
+  static constexpr bool kBf16 = false;
+  static __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+  }
+};
+
+template <typename O> __device__ __forceinline__ O to_out(float x);
+template <> __device__ __forceinline__ float to_out<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 to_out<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+template <> __device__ __forceinline__ __half to_out<__half>(float x) { return __float2half_rn(x); }
+
+// ---------------------------------------------------------------- schedule
+// Work is split in cost space.  In units where the K/V bytes of a full
+// 128-token tile cost kFullTile = 8, a tile also costs `tile_fixed` (its
+// fixed QK / softmax / PV work), a sequence's partial last tile costs its
+// 16-token boxes instead of 8, and every (sequence, KV head) pair costs
+// `seg` once (its set-up and epilogue).  Pairs are laid end to end
+// (b-major, then KV head); CTA c takes the tiles whose start cost lies in
+// [C*c/G, C*(c+1)/G).  Every tile belongs to exactly one CTA; a pair
+// spread over several CTAs is merged by the last of them.
+constexpr int kFullTile = 8;
+
+struct CostModel {
+  int tile_fixed, seg;
+  __device__ __forceinline__ int full() const { return kFullTile + tile_fixed; }
+  // cost of one pair of a sequence of `len` tokens
+  __device__ __forceinline__ int pair_cost(int len) const {
+    const int n_full = len / kTileTokens, rem = len % kTileTokens;
+    return seg + n_full * full() + ((rem > 0 || len == 0) ? (rem + 15) / 16 + tile_fixed : 0);
+  }
+};
+
+__device__ __forceinline__ int seq_tiles(int len) {
+  return len > 0 ? (len + kTileTokens - 1) / kTileTokens : 1;
+}
+
+__device__ __forceinline__ int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// One segment of a CTA's work: tiles tile0 .. tile0+ntiles-1 of pair (b, kvh).
+struct Segment {
+  int b, kvh, pair;
+  int tile0, ntiles;
+  int seqlen;
+  int nseg, cfirst;  // how many CTAs share this pair, and the first of them
+};
+
+struct Schedule {
+  const int* cost_prefix;  // [B+1] per-pair cost prefix over sequences (smem)
+  const int* lens;         // [B] sequence lengths, clamped to [0, max_len] (smem)
+  int64_t max_len, total;  // total = Hkv * cost_prefix[B]
+  int batch, hkv, grid;
+  CostModel cm;
+
+  __device__ __forceinline__ int len_of(int b) const { return lens[b]; }
+  __device__ __forceinline__ int64_t range_start(int c) const { return total * c / grid; }
+  // CTA whose range holds cost position s: largest c with range_start(c) <= s
+  __device__ __forceinline__ int cta_of(int64_t s) const {
+    return static_cast<int>(((s + 1) * grid + total - 1) / total - 1);
+  }
+  __device__ __forceinline__ int64_t pair_start(int pair) const {
+    const int b = pair / hkv, kvh = pair - b * hkv;
+    return static_cast<int64_t>(hkv) * cost_prefix[b] +
+           static_cast<int64_t>(kvh) * (cost_prefix[b + 1] - cost_prefix[b]);
+  }
+  __device__ __forceinline__ int64_t tile_start(int64_t cp, int j) const {
+    return j == 0 ? cp : cp + cm.seg + static_cast<int64_t>(j) * cm.full();
+  }
+  // Segment of `pair` from tile j0 on, cut at range end e1; false if no tile
+  // of the pair at or after j0 starts before e1.  Integer work here is 32-bit
+  // except for pairs split across CTAs (rare), where cta_of is evaluated.
+  __device__ __forceinline__ bool make(int pair, int j0, int64_t e1, Segment& s) const {
+    const int b = pair / hkv;
+    const int len = len_of(b);
+    const int n = seq_tiles(len);
+    const int64_t cp = pair_start(pair);
+    if (j0 >= n || tile_start(cp, j0) >= e1) return false;
+    // last tile with start < e1: j <= ceil((e1 - cp - seg) / full) - 1
+    const int64_t x64 = e1 - cp - cm.seg;
+    int jmax = 0;
+    if (x64 > 0) {
+      const int x = x64 < 0x7fffffff ? static_cast<int>(x64) : 0x7fffffff;
+      jmax = (x + cm.full() - 1) / cm.full() - 1;
+    }
+    if (jmax > n - 1) jmax = n - 1;
+    s.b = b;
+    s.kvh = pair - b * hkv;
+    s.pair = pair;
+    s.tile0 = j0;
+    s.ntiles = jmax - j0 + 1;
+    s.seqlen = len;
+    if (j0 == 0 && jmax == n - 1) {  // the whole pair lies in this range
+      s.nseg = 1;
+      s.cfirst = -1;
+    } else {
+      s.cfirst = cta_of(cp);
+      s.nseg = cta_of(tile_start(cp, n - 1)) - s.cfirst + 1;
+    }
+    return true;
+  }
+  // First segment of CTA c (false if the CTA has no tile).
+  __device__ __forceinline__ bool first(int c, Segment& s) const {
+    if (c >= grid) return false;
+    const int64_t e0 = range_start(c), e1 = range_start(c + 1);
+    int lo = 0, hi = batch - 1;  // largest b with hkv * prefix[b] <= e0
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (static_cast<int64_t>(hkv) * cost_prefix[mid] <= e0) lo = mid; else hi = mid - 1;
+    }
+    const int pc = cost_prefix[lo + 1] - cost_prefix[lo];
+    int kvh = static_cast<int>((e0 - static_cast<int64_t>(hkv) * cost_prefix[lo]) / pc);
+    kvh = kvh < hkv - 1 ? kvh : hkv - 1;
+    const int pair = lo * hkv + kvh;
+    const int64_t cp = pair_start(pair);
+    int j0 = 0;
+    if (e0 > cp) {
+      const int64_t x = e0 - cp - cm.seg;
+      j0 = static_cast<int>(x > 0 ? ceil_div64(x, cm.full()) : 1);
+      if (j0 < 1) j0 = 1;
+    }
+    if (make(pair, j0, e1, s)) return true;
+    return pair + 1 < batch * hkv && make(pair + 1, 0, e1, s);
+  }
+  // Segment after `s` within the range that ends at cost e1.
+  __device__ __forceinline__ bool next(const Segment& s, int64_t e1, Segment& nx) const {
+    if (s.tile0 + s.ntiles < seq_tiles(s.seqlen)) return false;  // range ended inside the pair
+    return s.pair + 1 < batch * hkv && make(s.pair + 1, 0, e1, nx);
+  }
+};
+
+__device__ __forceinline__ bool lane0_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                           uint64_t budget, int lane) {
+  int ok = 1;
+  if (lane == 0) ok = mbar_wait_bounded(bar, parity, abort_flag, budget) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+// MULTI = false: one query token per sequence, no causal mask (plain decode).
+// MULTI = true: seqlen_q query tokens, optional bottom-right causal mask.
+template <typename T, typename OutT, int NCOL, bool MULTI, bool XCHG>
+__global__ void __launch_bounds__(kSm100Threads, 1)
+    decode_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
+                        const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v,
+                        const __grid_constant__ CUtensorMap tm_k16,
+                        const __grid_constant__ CUtensorMap tm_v16, const DecodeParams p) {
+  // P.V uses N = 2*NCOL columns: NCOL hi parts then NCOL lo parts of P.
+  constexpr int kPvN = 2 * NCOL;
+  constexpr int kPGroupBytes = (kPvN / 8) * 128;  // one 8-token group of P rows
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+
+  // Stage s: K tile at +0, V tile at +32 KB, query rows at +64 KB.
+  uint8_t* stages = smem + kOffStages;
+  uint8_t* pbufs = smem + kOffP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
+  uint64_t* full = bars;            // stage loaded: K, V and query rows (two producers)
+  uint64_t* empty = bars + kStages;  // stage consumed: P.V of its tile done
+  uint64_t* s_full = bars + 2 * kStages;
+  uint64_t* s_empty = s_full + 2;
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* o_full = p_full + 2;
+  uint64_t* o_empty = o_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 8);
+  // Tiles of this CTA, published by the producer once its walk is done.
+  volatile int* tiles_total = reinterpret_cast<volatile int*>(smem + kOffMisc + 12);
+  float* red = reinterpret_cast<float*>(smem + kOffRed);
+  float* fin = reinterpret_cast<float*>(smem + kOffFin);
+  int* prefix = reinterpret_cast<int*>(smem + kOffPrefix);
+  int* lens = reinterpret_cast<int*>(smem + kOffLens);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int batch = p.batch;
+  const int hkv = p.num_heads_k;
+  const int group = p.group;
+  const int sq = MULTI ? p.seqlen_q : 1;  // query tokens per sequence
+  const int qrows = p.qrows;   // query rows per (sequence, KV head): sq * group <= 16
+  const uint64_t budget = p.timeout_ns;
+  const int64_t max_len = p.bt_stride * static_cast<int64_t>(p.page);
+
+  // ------------------------------------------------------------ prologue
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 2);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], 128);
+    }
+    *abort_flag = 0;
+    *last_flag = 0;
+    *tiles_total = 0x7fffffff;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  // Zero the stages' query areas (rows >= qrows stay zero: the query TMA
+  // writes rows < qrows only) and the P buffers (columns >= qrows stay zero).
+  for (int s = 0; s < kStages; ++s) {
+    uint4* z = reinterpret_cast<uint4*>(stages + s * kStageBytes + 2 * kOperandBytes);
+    for (int i = tid; i < kQSlotBytes / 16; i += kSm100Threads) z[i] = make_uint4(0, 0, 0, 0);
+  }
+  {
+    uint4* z = reinterpret_cast<uint4*>(pbufs);
+    for (int i = tid; i < 2 * kPBufBytes / 16; i += kSm100Threads) z[i] = make_uint4(0, 0, 0, 0);
+  }
+  const CostModel cm{p.cost_tile, p.cost_seg};
+  for (int b = tid; b < batch; b += kSm100Threads) {
+    int len = __ldg(p.seqlens + b);
+    len = len < 0 ? 0 : len;
+    len = static_cast<int>(len > max_len ? max_len : len);
+    lens[b] = len;
+    prefix[b + 1] = cm.pair_cost(len);
+  }
+  if (tid == 0) prefix[0] = 0;
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) {  // inclusive scan of pair costs -> exclusive prefix sums
+    int carry = 0;
+    for (int base = 1; base <= batch; base += 32) {
+      const int idx = base + lane;
+      int v = idx <= batch ? prefix[idx] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+      }
+      v += carry;
+      if (idx <= batch) prefix[idx] = v;
+      carry = __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
+  __syncthreads();
+
+  const uint32_t tmem = *tmem_slot;
+  const int cta = blockIdx.x;
+  Schedule sched;
+  sched.cost_prefix = prefix;
+  sched.lens = lens;
+  sched.max_len = max_len;
+  sched.total = static_cast<int64_t>(hkv) * prefix[batch];
+  sched.batch = batch;
+  sched.hkv = hkv;
+  sched.cm = cm;
+  // Each CTA's cost range is longer than the costliest tile (seg + full), so
+  // every range holds at least one tile start: no CTA inside a pair's span is
+  // empty, which the nseg count relies on.  CTAs past that (the host sized
+  // the grid from an upper bound) have nothing to do.
+  {
+    const int64_t g = sched.total / (cm.seg + cm.full() + 1);
+    sched.grid = static_cast<int>(g < 1 ? 1 : (g < gridDim.x ? g : gridDim.x));
+  }
+  const int64_t range_end = sched.range_start(cta + 1);
+
+  if (warp == 0 || warp == kVProducerWarp) {
+    // ---------------------------------------------------------- TMA producers
+    // Warp 0 issues the K boxes and the group's query rows of each stage,
+    // warp 6 its V boxes; both arrive on the stage's `full` barrier.  Two
+    // issuing warps halve the per-stage TMA issue time, which matters for
+    // small pages (16-token boxes: 16 per operand per tile).
+    const bool is_v = warp == kVProducerWarp;
+    if (lane == 0) {
+      if (is_v) {
+        tma_prefetch_desc(&tm_v);
+        tma_prefetch_desc(&tm_v16);
+      } else {
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_k16);
+      }
+    }
+    uint64_t* ring_full = full;
+    uint64_t* ring_empty = empty;
+    const CUtensorMap* map_full = is_v ? &tm_v : &tm_k;
+    const CUtensorMap* map_tail = is_v ? &tm_v16 : &tm_k16;
+    const int operand_off = is_v ? kOperandBytes : 0;
+    const uint32_t extra_tx = is_v ? 0u : 2u * qrows * 128u;  // query rows ride with K
+    const uint64_t pol_stream = policy_evict_first();
+    const uint64_t pol_keep = policy_evict_last();
+    const int chunk = p.chunk;  // tokens per TMA box of a full tile; never crosses a page
+    const int nchunks = kTileTokens / chunk;
+    int64_t it = 0;
+    bool ok = true;
+    Segment s;
+    for (bool have = sched.first(cta, s); have && ok; have = sched.next(s, range_end, s)) {
+      const int32_t* bt_row = p.block_table + static_cast<int64_t>(s.b) * p.bt_stride;
+      for (int t = 0; t < s.ntiles; ++t, ++it) {
+        const int tok0 = (s.tile0 + t) * kTileTokens;
+        const int valid_rows = s.seqlen - tok0;
+        // Full tile: `nchunks` boxes of `chunk` tokens.  Last partial tile:
+        // 16-token boxes over the valid rows only.
+        const bool tail = valid_rows < kTileTokens;
+        const int box = tail ? 16 : chunk;
+        const int nbox = tail ? (valid_rows > 0 ? (valid_rows + 15) / 16 : 0) : nchunks;
+        const int pos = tok0 + lane * box;
+        const bool need = lane < nbox;
+        int page_id = 0;
+        if (need) page_id = __ldg(bt_row + pos / p.page);  // issued before the wait
+        const int stage = static_cast<int>(it % kStages);
+        ok = lane0_wait(&ring_empty[stage], static_cast<uint32_t>((it / kStages) & 1) ^ 1u,
+                        abort_flag, budget, lane);
+        if (!ok) break;
+        uint8_t* sdst = stages + stage * kStageBytes;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&ring_full[stage], static_cast<uint32_t>(nbox * box) * 256u + extra_tx);
+          if (!is_v) {
+            uint8_t* qdst = sdst + 2 * kOperandBytes;
+            // rows qi * group + g: query token qi, head kvh * group + g
+            tma_load_4d(&tm_q, &ring_full[stage], qdst, 0, s.kvh * group, 0, s.b, pol_keep);
+            tma_load_4d(&tm_q, &ring_full[stage], qdst + kQSlotBytes / 2, 64, s.kvh * group, 0, s.b,
+                        pol_keep);
+          }
+        }
+        __syncwarp();
+        if (need) {
+          const int off = pos % p.page;
+          const CUtensorMap* m = tail ? map_tail : map_full;
+          uint8_t* dst = sdst + operand_off + lane * box * 128;
+          tma_load_4d(m, &ring_full[stage], dst, 0, s.kvh, off, page_id, pol_stream);
+          tma_load_4d(m, &ring_full[stage], dst + kHalfBytes, 64, s.kvh, off, page_id, pol_stream);
+        }
+        __syncwarp();
+      }
+    }
+    if (!is_v && lane == 0) *tiles_total = static_cast<int>(it);
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- UMMA issuer
+    // Tiles 0 .. ntiles-1 of this CTA's range.  QK(i) needs stage i loaded
+    // and S buffer i%2 drained; PV(i) needs P(i) written and O buffer i%2
+    // drained.  Whichever is ready is issued (PV first: it frees a stage).
+    constexpr bool kBf16 = DType<T>::kBf16;
+    constexpr uint32_t idesc_qk = make_idesc(kBf16, false, false, 128, kMaxGroup);
+    constexpr uint32_t idesc_pv = make_idesc(kBf16, true, true, 128, kPvN);
+    int64_t qk = 0, pv = 0;
+    uint64_t idle_since = 0;
+    uint32_t spins = 0;
+    while (true) {
+      int action = 0;  // 1 = PV, 2 = QK, 3 = abort, 4 = all tiles done
+      if (lane == 0) {
+        const int64_t ntiles = *tiles_total;  // the producer's count once known
+        if (pv >= ntiles) action = 4;
+        if (action == 0 && pv < qk) {
+          const int pb = static_cast<int>(pv & 1);
+          const uint32_t ph = static_cast<uint32_t>((pv >> 1) & 1);
+          if (mbar_test_wait(&p_full[pb], ph) && mbar_test_wait(&o_empty[pb], ph ^ 1u)) action = 1;
+        }
+        if (action == 0 && qk < ntiles) {
+          const int st = static_cast<int>(qk % kStages);
+          if (mbar_test_wait(&full[st], static_cast<uint32_t>((qk / kStages) & 1)) &&
+              mbar_test_wait(&s_empty[qk & 1], static_cast<uint32_t>(((qk >> 1) & 1) ^ 1)))
+            action = 2;
+        }
+        if (action == 0) {
+          if (((++spins) & 255u) == 0u) {
+            const uint64_t now = globaltimer_ns();
+            if (idle_since == 0) idle_since = now;
+            if (*abort_flag || now - idle_since > budget) {
+              *abort_flag = 1;
+              action = 3;
+            }
+          }
+        } else {
+          idle_since = 0;
+        }
+      }
+      action = __shfl_sync(0xffffffffu, action, 0);
+      if (action >= 3) break;
+      if (action == 0) continue;
+      tc_fence_after();
+      if (lane == 0) {
+        if (action == 1) {
+          const int pb = static_cast<int>(pv & 1);
+          const int stage = static_cast<int>(pv % kStages);
+          const uint32_t vaddr = smem_u32(stages + stage * kStageBytes + kOperandBytes);
+          const uint32_t paddr = smem_u32(pbufs + pb * kPBufBytes);
+#pragma unroll
+          for (int j = 0; j < kTileTokens / 16; ++j) {
+            // A = V^T: MN-major (head-dim contiguous), 128B swizzle; the two
+            // 64-dim halves are 16 KB apart (LBO), 8-token groups 1 KB apart (SBO).
+            const uint64_t a = make_sdesc(vaddr + j * 2048, kHalfBytes, 1024, kLayoutSw128);
+            // B = [P_hi | P_lo]^T: MN-major (heads contiguous), no swizzle;
+            // 8-column core matrices 128 B apart (SBO), 8-token groups kPGroupBytes apart (LBO).
+            const uint64_t b = make_sdesc(paddr + j * 2 * kPGroupBytes, kPGroupBytes, 128, kLayoutNone);
+            umma_f16(tmem + col_o(pb), a, b, idesc_pv, j > 0 ? 1u : 0u);
+          }
+          umma_commit(&o_full[pb]);
+          umma_commit(&empty[stage]);
+        } else {
+          const int st = static_cast<int>(qk % kStages);
+          const int sb = static_cast<int>(qk & 1);
+          const uint32_t kaddr = smem_u32(stages + st * kStageBytes);
+          const uint32_t qaddr = kaddr + 2 * kOperandBytes;
+#pragma unroll
+          for (int j = 0; j < kHeadDim / 16; ++j) {
+            // A = K tile, K-major 128B swizzle: 8-row groups 1 KB apart; the
+            // 16-dim step j moves 32 B inside a 128 B row, 64-dim halves 16 KB apart.
+            const uint64_t a =
+                make_sdesc(kaddr + (j >> 2) * kHalfBytes + (j & 3) * 32, 16, 1024, kLayoutSw128);
+            const uint64_t b = make_sdesc(qaddr + (j >> 2) * (kQSlotBytes / 2) + (j & 3) * 32, 16,
+                                          1024, kLayoutSw128);
+            umma_f16(tmem + col_s(sb), a, b, idesc_qk, j > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[sb]);
+        }
+      }
+      __syncwarp();
+      if (action == 1) ++pv; else ++qk;
+    }
+  } else {
+    // ---------------------------------------------------------- softmax warps
+    // One flat loop over the CTA's tiles.  Iteration i runs the softmax of
+    // tile i, then folds in O of tile i-1.  When tile i opens a new segment,
+    // O of the previous segment's last tile arrives in that same iteration
+    // and the previous segment is finished there, so the P.V round trip of a
+    // segment's last tile overlaps the next segment's first softmax.
+    const int quad = warp & 3;         // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;  // token row of S, head-dim index of O
+    const int d = row;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const float neg_inf = -__int_as_float(0x7f800000);
+    const int hq = p.num_heads;
+    OutT* out = reinterpret_cast<OutT*>(p.out);
+    struct State {
+      float m[NCOL], l[NCOL], o[NCOL], a[NCOL];
+    };
+    auto reset = [&](State& st) {
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) {
+        st.m[h] = neg_inf;
+        st.l[h] = 0.f;
+        st.o[h] = 0.f;
+        st.a[h] = 0.f;
+      }
+    };
+    // O^T of tile i (hi + lo halves) for this thread's head-dim row.
+    auto load_o = [&](int64_t i, float (&ov)[NCOL]) {
+      const int pb = static_cast<int>(i & 1);
+      mbar_wait_bounded(&o_full[pb], static_cast<uint32_t>((i >> 1) & 1), abort_flag, budget);
+      tc_fence_after();
+      uint32_t r[kPvN];
+      if constexpr (NCOL == 8) tmem_ld_x16(lane_addr + col_o(pb), r); else tmem_ld_x32(lane_addr + col_o(pb), r);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&o_empty[pb]);
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) ov[h] = __uint_as_float(r[h]) + __uint_as_float(r[NCOL + h]);
+    };
+    // Segment epilogue: direct output, or partial + (last arrival) merge.
+    int fin_buf = 0;
+    // `scratch`: a P buffer no P.V is reading (used when merging a split pair).
+    auto finish = [&](const Segment& sg, const State& st, uint8_t* scratch) {
+      float* fb = fin + fin_buf * (4 * kMaxGroup);
+      fin_buf ^= 1;
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) {
+        float v = st.l[h];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) fb[quad * kMaxGroup + h] = v;
+      }
+      named_bar_sync(1, 128);
+      float l_tot[NCOL];
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h)
+        l_tot[h] = (fb[h] + fb[kMaxGroup + h]) + (fb[2 * kMaxGroup + h] + fb[3 * kMaxGroup + h]);
+      // column h = query row (qi, g): token qi of the sequence's sq new
+      // tokens, query head kvh * group + g
+      auto out_index = [&](int h) {
+        const int qi = MULTI ? h / group : 0, g = h - qi * group;
+        return ((static_cast<int64_t>(sg.b) * sq + qi) * hq + sg.kvh * group + g) * kHeadDim + d;
+      };
+      auto lse_index = [&](int h) {
+        const int qi = MULTI ? h / group : 0, g = h - qi * group;
+        return (static_cast<int64_t>(sg.b) * hq + sg.kvh * group + g) * sq + qi;
+      };
+      // Result writers: the output (and LSE), or, in a cross-GPU exchange,
+      // this rank's part in every rank's exchange buffer.
+      auto put_o = [&](int64_t oi, float v) {
+        if constexpr (XCHG) {
+          for (int j = 0; j < p.xworld; ++j) p.xpart[j][oi] = v;
+        } else {
+          out[oi] = to_out<OutT>(v);
+        }
+      };
+      auto put_lse = [&](int64_t li, float v) {
+        if constexpr (XCHG) {
+          for (int j = 0; j < p.xworld; ++j) p.xpart[j][p.xlse_off + li] = v;
+        } else if (p.lse != nullptr) {
+          p.lse[li] = v;
+        }
+      };
+      if (sg.nseg == 1) {
+#pragma unroll
+        for (int h = 0; h < NCOL; ++h) {
+          if (h < qrows) {
+            const float v = l_tot[h] > 0.f ? st.o[h] / l_tot[h] : 0.f;
+            put_o(out_index(h), v);
+            if (d == h)
+              put_lse(lse_index(h),
+                      l_tot[h] > 0.f ? (st.m[h] + fast_log2(l_tot[h])) * 0.69314718055994531f : neg_inf);
+          }
+        }
+        return;
+      }
+      const int64_t slot = static_cast<int64_t>(cta) + sg.pair;
+      float* po = p.part_o + slot * qrows * kHeadDim + d;
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) {
+        if (h < qrows) {
+          po[h * kHeadDim] = l_tot[h] > 0.f ? st.o[h] / l_tot[h] : 0.f;
+          if (d == h) p.part_lse[slot * qrows + h] = l_tot[h] > 0.f ? st.m[h] + fast_log2(l_tot[h]) : neg_inf;
+        }
+      }
+      __threadfence();
+      named_bar_sync(1, 128);
+      if (d == 0) {
+        int is_last = 0;
+        if (!*abort_flag) is_last = ticket_arrive(p.tickets + sg.pair, p.epoch, sg.nseg) ? 1 : 0;
+        *last_flag = is_last;
+      }
+      named_bar_sync(1, 128);
+      const int merge = *last_flag;
+      named_bar_sync(1, 128);  // last_flag is reused by the next split segment
+      if (!merge) return;
+      __threadfence();
+      const int64_t sbase = static_cast<int64_t>(sg.cfirst) + sg.pair;
+      // The pair's nseg x qrows partial LSEs are contiguous: stage them in a
+      // free P buffer with one parallel load, so the per-head weights come
+      // from shared memory and only the independent partial-O loads remain.
+      const int nl = sg.nseg * qrows;
+      float* sl = reinterpret_cast<float*>(scratch);
+      const bool staged = nl <= kPBufBytes / 4;
+      if (staged) {
+        for (int i = d; i < nl; i += 128) sl[i] = __ldcg(p.part_lse + sbase * qrows + i);
+        named_bar_sync(1, 128);
+      }
+      for (int h = 0; h < qrows; ++h) {
+        auto lse_of = [&](int j) {
+          return staged ? sl[j * qrows + h] : __ldcg(p.part_lse + (sbase + j) * qrows + h);
+        };
+        float mx = neg_inf;
+        for (int j = 0; j < sg.nseg; ++j) mx = fmaxf(mx, lse_of(j));
+        float den = 0.f, acc = 0.f;
+#pragma unroll 4
+        for (int j = 0; j < sg.nseg; ++j) {
+          const float lj = lse_of(j);
+          const float wj = lj == neg_inf ? 0.f : fast_exp2(lj - mx);  // empty parts hold O = 0
+          acc = fmaf(wj, __ldcg(p.part_o + ((sbase + j) * qrows + h) * kHeadDim + d), acc);
+          den += wj;
+        }
+        put_o(out_index(h), den > 0.f ? acc / den : 0.f);
+        if (d == 0) put_lse(lse_index(h), den > 0.f ? (mx + fast_log2(den)) * 0.69314718055994531f : neg_inf);
+      }
+    };
+
+    // Per query row h = (qi, g): how many of the sequence's last keys it may
+    // not see (0 unless causal): key t is visible iff t < L + coff[h].
+    int coff[NCOL];
+#pragma unroll
+    for (int h = 0; h < NCOL; ++h) coff[h] = (MULTI && p.causal) ? (h / group) - (sq - 1) : 0;
+
+    State cur, prev;
+    reset(cur);
+    reset(prev);
+    Segment seg{}, prev_seg{};
+    int t = 0;
+    int64_t it = 0;
+    for (bool have = sched.first(cta, seg); have; ++it, ++t) {
+      bool prev_open = false;
+      if (t == seg.ntiles) {  // next segment, if the range has one
+        Segment nx;
+        if (!sched.next(seg, range_end, nx)) break;
+        prev_seg = seg;
+        seg = nx;
+        t = 0;
+        prev = cur;
+        reset(cur);
+        prev_open = true;
+      }
+      // ---- softmax of tile `it`
+      const int sb = static_cast<int>(it & 1);
+      const int stage = static_cast<int>(it % kStages);
+      mbar_wait_bounded(&s_full[sb], static_cast<uint32_t>((it >> 1) & 1), abort_flag, budget);
+      tc_fence_after();
+      uint32_t r[NCOL];
+      if constexpr (NCOL == 8) tmem_ld_x8(lane_addr + col_s(sb), r); else tmem_ld_x16(lane_addr + col_s(sb), r);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);
+
+      const int tok0 = (seg.tile0 + t) * kTileTokens;
+      const int valid_rows = seg.seqlen - tok0;  // may exceed 128; <=0 only for empty sequences
+      const bool valid = row < valid_rows;
+      float sv[NCOL];
+      float* red_t = red + (it & 1) * (4 * kMaxGroup);
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) {
+        // causal: query row h sees keys up to its own position L - sq + qi
+        const bool vis = MULTI ? row < valid_rows + coff[h] : valid;
+        sv[h] = vis ? __uint_as_float(r[h]) * p.scale_log2 : neg_inf;
+        const float wm = warp_max_f32(sv[h]);
+        if (lane == 0) red_t[quad * kMaxGroup + h] = wm;
+      }
+      named_bar_sync(1, 128);
+      float pv[NCOL], alpha[NCOL];
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) {
+        const float tmax = fmaxf(fmaxf(red_t[h], red_t[kMaxGroup + h]),
+                                 fmaxf(red_t[2 * kMaxGroup + h], red_t[3 * kMaxGroup + h]));
+        const float m_new = fmaxf(cur.m[h], tmax);
+        const float m_use = m_new == neg_inf ? 0.f : m_new;
+        alpha[h] = fast_exp2(cur.m[h] - m_use);
+        pv[h] = (h < qrows) ? fast_exp2(sv[h] - m_use) : 0.f;
+        cur.l[h] = fmaf(cur.l[h], alpha[h], pv[h]);
+        cur.m[h] = m_new;
+      }
+      if (valid_rows < kTileTokens && !valid) {
+        // Rows past the sequence end: stale or never-written data must not
+        // reach P.V (0 * NaN), so zero this token's V row in the stage.
+        uint4* vrow0 = reinterpret_cast<uint4*>(stages + stage * kStageBytes + kOperandBytes + row * 128);
+        uint4* vrow1 = reinterpret_cast<uint4*>(stages + stage * kStageBytes + kOperandBytes + kHalfBytes + row * 128);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          vrow0[i] = make_uint4(0, 0, 0, 0);
+          vrow1[i] = make_uint4(0, 0, 0, 0);
+        }
+      }
+      {
+        // This token's row of [P_hi | P_lo]: 8-column chunks 128 B apart.
+        uint8_t* prow = pbufs + sb * kPBufBytes + (row >> 3) * kPGroupBytes + (row & 7) * 16;
+#pragma unroll
+        for (int c = 0; c < NCOL / 8; ++c) {
+          uint4 hi, lo;
+          DType<T>::split2(pv[8 * c + 0], pv[8 * c + 1], hi.x, lo.x);
+          DType<T>::split2(pv[8 * c + 2], pv[8 * c + 3], hi.y, lo.y);
+          DType<T>::split2(pv[8 * c + 4], pv[8 * c + 5], hi.z, lo.z);
+          DType<T>::split2(pv[8 * c + 6], pv[8 * c + 7], hi.w, lo.w);
+          *reinterpret_cast<uint4*>(prow + c * 128) = hi;
+          *reinterpret_cast<uint4*>(prow + (NCOL / 8 + c) * 128) = lo;
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&p_full[sb]);
+
+      // ---- O of tile it-1
+      if (it > 0) {
+        float ov[NCOL];
+        load_o(it - 1, ov);
+        if (prev_open) {
+#pragma unroll
+          for (int h = 0; h < NCOL; ++h) prev.o[h] = fmaf(prev.o[h], prev.a[h], ov[h]);
+          // P.V(it-1) is done, so its P buffer is free until tile it+1's softmax
+          finish(prev_seg, prev, pbufs + ((it + 1) & 1) * kPBufBytes);
+        } else {
+#pragma unroll
+          for (int h = 0; h < NCOL; ++h) cur.o[h] = fmaf(cur.o[h], cur.a[h], ov[h]);
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) cur.a[h] = alpha[h];
+    }
+    if (it > 0) {
+      float ov[NCOL];
+      load_o(it - 1, ov);
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) cur.o[h] = fmaf(cur.o[h], cur.a[h], ov[h]);
+      finish(seg, cur, pbufs);  // every P.V is done
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (XCHG && tid == 0 && !*abort_flag) {
+    // After the CTA barrier, one system-scope fence publishes the CTA's
+    // exchange writes; the CTA that finishes last on this GPU then tells
+    // every rank that this rank's part is complete (the host zeroes xdone
+    // before each launch).
+    __threadfence_system();
+    if (atomicAdd(p.xdone, 1u) == gridDim.x - 1u) {
+      __threadfence_system();
+      for (int j = 0; j < p.xworld; ++j) st_release_sys_u32(p.xflag[j], p.xepoch);
+    }
+  }
+  if (*abort_flag) {
+    if (tid == 0) {
+      atomicExch(p.err, 5);
+      // Let any copy or MMA still in flight land before the CTA's shared
+      // memory and TMEM are released (bounded: 2 ms).
+      const uint64_t t0 = globaltimer_ns();
+      while (globaltimer_ns() - t0 < 2000000ull) {
+      }
+    }
+    __syncthreads();
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <typename T, typename OutT, int NCOL, bool MULTI, bool XCHG = false>
+cudaError_t launch_typed(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream) {
+  auto kern = decode_sm100_kernel<T, OutT, NCOL, MULTI, XCHG>;
+  // The attribute is per device; setting it again is harmless.
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if ((__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & bit) == 0) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
+  }
+  kern<<<grid, kSm100Threads, kSmemBytes, stream>>>(m.q, m.k, m.v, m.k16, m.v16, p);
+  return cudaGetLastError();
+}
+
+template <typename T, typename OutT>
+cudaError_t launch_ncol(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream) {
+  const bool multi = p.seqlen_q > 1 || p.causal;
+  if constexpr (std::is_same<OutT, float>::value) {
+    if (p.xworld > 0) {  // cross-GPU exchange: fp32 parts to every rank
+      if (p.qrows <= 8)
+        return multi ? launch_typed<T, float, 8, true, true>(m, p, grid, stream)
+                     : launch_typed<T, float, 8, false, true>(m, p, grid, stream);
+      return multi ? launch_typed<T, float, 16, true, true>(m, p, grid, stream)
+                   : launch_typed<T, float, 16, false, true>(m, p, grid, stream);
+    }
+  }
+  if (p.qrows <= 8)
+    return multi ? launch_typed<T, OutT, 8, true>(m, p, grid, stream)
+                 : launch_typed<T, OutT, 8, false>(m, p, grid, stream);
+  return multi ? launch_typed<T, OutT, 16, true>(m, p, grid, stream)
+               : launch_typed<T, OutT, 16, false>(m, p, grid, stream);
+}
+
+}  // namespace
+
+}  // namespace fd

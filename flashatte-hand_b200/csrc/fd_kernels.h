@@ -72,6 +72,12 @@ struct TensorMaps {
   CUtensorMap q, k, v, k16, v16;
 };
 
+// Per-dtype instantiations of the tensor-core kernel (one translation unit each).
+cudaError_t launch_sm100_bf16(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
+cudaError_t launch_sm100_bf16_f32(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
+cudaError_t launch_sm100_fp16(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
+cudaError_t launch_sm100_fp16_f32(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
+
 // Launchers.  dtype: 0 bf16, 1 fp16; out_fp32 selects an fp32 output.
 cudaError_t launch_decode_sm100(const TensorMaps& m, const DecodeParams& p, int dtype,
                                 bool out_fp32, int grid, cudaStream_t stream);
