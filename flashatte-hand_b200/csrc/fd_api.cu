@@ -162,6 +162,14 @@ int cost_seg() {
   return v;
 }
 
+// Programmatic dependent launch of the decode kernel (FD_PDL=0 turns it off):
+// its prologue may overlap the previous kernel on the stream; it reads no
+// input before that kernel has completed.
+bool pdl_enabled() {
+  static const bool v = env_int("FD_PDL", 1, 0, 1) != 0;
+  return v;
+}
+
 unsigned long long timeout_ns() {
   static unsigned long long v = [] {
     const char* e = std::getenv("FD_WAIT_TIMEOUT_NS");
@@ -244,8 +252,8 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
                 int64_t block_table_stride, int64_t batch_size, int64_t seqlen_q, int64_t num_heads,
                 int64_t num_heads_k, int64_t headdim, int64_t page_block_size, int64_t num_blocks,
                 int dtype, int out_dtype, float softmax_scale, int causal, int64_t max_seqlen_k,
-                void* workspace, size_t workspace_bytes, void* stream, const ExchangeArgs* xa,
-                int** err_word) {
+                int len_add, void* workspace, size_t workspace_bytes, void* stream,
+                const ExchangeArgs* xa, int** err_word) {
   if (xa != nullptr) out = xa->part[0];  // results go to the exchange parts
   if (q == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr ||
       cache_seqlens == nullptr || block_table == nullptr)
@@ -299,7 +307,7 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
     sp.num_heads_k = static_cast<int>(num_heads_k); sp.group = group;
     sp.head_dim = static_cast<int>(headdim); sp.page = static_cast<int>(page_block_size);
     sp.seqlen_q = static_cast<int>(seqlen_q); sp.causal = causal ? 1 : 0;
-    sp.num_blocks = num_blocks; sp.scale_log2 = scale_log2;
+    sp.num_blocks = num_blocks; sp.scale_log2 = scale_log2; sp.len_add = len_add;
     const int vec = static_cast<int>(headdim / 32) * 2;  // bytes per lane load
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_cache) |
          reinterpret_cast<uintptr_t>(v_cache)) % vec != 0)
@@ -390,6 +398,8 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
     p.cost_tile = cost_tile();
     p.cost_seg = cost_seg();
     p.xworld = 0;
+    p.pdl = (xa == nullptr && pdl_enabled()) ? 1 : 0;
+    p.len_add = len_add;
     if (xa != nullptr) {
       p.xworld = xa->world;
       for (int j = 0; j < fd::kMaxExchangeRanks; ++j) {
@@ -424,7 +434,7 @@ int fd_decode_paged_mq(const void* q, const void* k_cache, const void* v_cache, 
                        size_t workspace_bytes, void* stream) {
   return decode_impl(q, k_cache, v_cache, out, lse, cache_seqlens, block_table, block_table_stride,
                      batch_size, seqlen_q, num_heads, num_heads_k, headdim, page_block_size,
-                     num_blocks, dtype, out_dtype, softmax_scale, causal, max_seqlen_k, workspace,
+                     num_blocks, dtype, out_dtype, softmax_scale, causal, max_seqlen_k, 0, workspace,
                      workspace_bytes, stream, nullptr, nullptr);
 }
 
@@ -510,7 +520,7 @@ int fd_decode_paged_xgpu(const void* q, const void* k_cache, const void* v_cache
   const int st = decode_impl(q, k_cache, v_cache, nullptr, nullptr, cache_seqlens, block_table,
                              block_table_stride, batch_size, seqlen_q, num_heads, num_heads_k,
                              headdim, page_block_size, num_blocks, dtype, FD_DTYPE_FP32,
-                             softmax_scale, causal, max_seqlen_k, workspace, workspace_bytes,
+                             softmax_scale, causal, max_seqlen_k, 0, workspace, workspace_bytes,
                              stream, &xa, &err);
   if (st != FD_OK) return st;
   uint8_t* mine = static_cast<uint8_t*>(xbufs[rank]);
@@ -522,6 +532,72 @@ int fd_decode_paged_xgpu(const void* q, const void* k_cache, const void* v_cache
       static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "exchange combine: %s", cudaGetErrorString(e));
   return set_ok();
+}
+
+int fd_append_kv_paged(const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                       const int32_t* cache_seqlens, const int32_t* block_table,
+                       int64_t block_table_stride, int64_t batch_size, int64_t seqlen_new,
+                       int64_t num_heads_k, int64_t headdim, int64_t page_block_size,
+                       int64_t num_blocks, int dtype, void* stream) {
+  if (k_new == nullptr || v_new == nullptr || k_cache == nullptr || v_cache == nullptr ||
+      cache_seqlens == nullptr || block_table == nullptr)
+    return set_error(FD_ERR_INVALID_ARG, "null tensor pointer");
+  if (batch_size <= 0 || seqlen_new <= 0 || num_heads_k <= 0 || headdim <= 0 ||
+      page_block_size <= 0 || num_blocks <= 0 || block_table_stride <= 0)
+    return set_error(FD_ERR_INVALID_ARG, "sizes must be positive");
+  if (dtype != FD_DTYPE_BF16 && dtype != FD_DTYPE_FP16)
+    return set_error(FD_ERR_INVALID_ARG, "dtype must be bf16 or fp16");
+  if (seqlen_new > 65535 || batch_size * seqlen_new > INT32_MAX || page_block_size > INT32_MAX ||
+      num_heads_k * headdim > INT32_MAX)
+    return set_error(FD_ERR_UNSUPPORTED, "size exceeds 32-bit index range");
+  fd::AppendParams ap;
+  ap.k_new = k_new; ap.v_new = v_new; ap.k_cache = k_cache; ap.v_cache = v_cache;
+  ap.seqlens = cache_seqlens; ap.block_table = block_table;
+  ap.bt_stride = block_table_stride; ap.num_blocks = num_blocks;
+  ap.batch = static_cast<int>(batch_size); ap.seqlen_new = static_cast<int>(seqlen_new);
+  ap.num_heads_k = static_cast<int>(num_heads_k); ap.head_dim = static_cast<int>(headdim);
+  ap.page = static_cast<int>(page_block_size); ap.elem_bytes = esize(dtype);
+  ap.skipped = nullptr;
+  const cudaError_t e = fd::launch_append_kv(ap, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "append launch: %s", cudaGetErrorString(e));
+  return set_ok();
+}
+
+int fd_decode_paged_kvappend(const void* q, void* k_cache, void* v_cache, const void* k_new,
+                             const void* v_new, void* out, float* lse,
+                             const int32_t* cache_seqlens, const int32_t* block_table,
+                             int64_t block_table_stride, int64_t batch_size, int64_t seqlen_q,
+                             int64_t seqlen_new, int64_t num_heads, int64_t num_heads_k,
+                             int64_t headdim, int64_t page_block_size, int64_t num_blocks,
+                             int dtype, int out_dtype, float softmax_scale, int causal,
+                             int64_t max_seqlen_k, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  // Check what the attention half would reject before the cache is written.
+  if (q == nullptr || out == nullptr) return set_error(FD_ERR_INVALID_ARG, "null tensor pointer");
+  if (seqlen_q <= 0 || num_heads <= 0 || num_heads_k <= 0 || num_heads % num_heads_k != 0)
+    return set_error(FD_ERR_INVALID_ARG, "bad head counts or seqlen_q");
+  if (headdim != 32 && headdim != 64 && headdim != 128 && headdim != 256)
+    return set_error(FD_ERR_UNSUPPORTED, "head dim %lld not in {32, 64, 128, 256}",
+                     (long long)headdim);
+  if (out_dtype != dtype && out_dtype != FD_DTYPE_FP32)
+    return set_error(FD_ERR_INVALID_ARG, "out_dtype must equal dtype or be fp32");
+  if (!std::isfinite(softmax_scale))
+    return set_error(FD_ERR_INVALID_ARG, "softmax_scale must be finite");
+  if (batch_size * seqlen_q * num_heads > INT32_MAX || seqlen_q > 65535 || num_heads > 65535)
+    return set_error(FD_ERR_UNSUPPORTED, "size exceeds 32-bit index range");
+  if (workspace != nullptr &&
+      workspace_bytes < fd_decode_workspace_size_mq(batch_size, seqlen_q, num_heads, num_heads_k,
+                                                    headdim))
+    return set_error(FD_ERR_WORKSPACE, "workspace too small");
+  const int st = fd_append_kv_paged(k_new, v_new, k_cache, v_cache, cache_seqlens, block_table,
+                                    block_table_stride, batch_size, seqlen_new, num_heads_k,
+                                    headdim, page_block_size, num_blocks, dtype, stream);
+  if (st != FD_OK) return st;
+  return decode_impl(q, k_cache, v_cache, out, lse, cache_seqlens, block_table, block_table_stride,
+                     batch_size, seqlen_q, num_heads, num_heads_k, headdim, page_block_size,
+                     num_blocks, dtype, out_dtype, softmax_scale, causal, max_seqlen_k,
+                     static_cast<int>(seqlen_new), workspace, workspace_bytes, stream, nullptr,
+                     nullptr);
 }
 
 int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, void* out, float* lse,

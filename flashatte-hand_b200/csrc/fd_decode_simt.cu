@@ -52,10 +52,11 @@ __global__ void __launch_bounds__(32 * kSimtWarps)
   const int kvh = h / p.group;
   const float neg_inf = -__int_as_float(0x7f800000);
 
-  int len = p.seqlens[b];
-  len = len < 0 ? 0 : len;
+  const int stored = p.seqlens[b];
+  const int64_t want = static_cast<int64_t>(stored < 0 ? 0 : stored) + p.len_add;
   const int64_t max_len = p.bt_stride * static_cast<int64_t>(p.page);
-  if (len > max_len) len = static_cast<int>(max_len);
+  const int64_t cap = max_len < 0x7fffffff ? max_len : 0x7fffffff;
+  int len = static_cast<int>(want > cap ? cap : want);
   // bottom-right causal mask: query token qi sits at position L - sq + qi
   if (p.causal) len = len - (p.seqlen_q - 1 - qi);
   if (len < 0) len = 0;

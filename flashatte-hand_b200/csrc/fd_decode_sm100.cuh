@@ -17,13 +17,13 @@
 // Per tile the CTA runs, warp-specialised:
 //   warps 0,6 TMA producers: gather the tile's K (warp 0, with the group's
 //             query rows) and V (warp 6) rows page by page through
-//             block_table into a 3-deep shared-memory ring (128B-swizzled,
+//             block_table into 3-deep shared-memory rings (128B-swizzled,
 //             two 64-dim halves); a sequence's last, partial tile is fetched
 //             in 16-token boxes covering only its valid rows.
-//   warp 1    tcgen05 issuer: S^T[tok, head] = K . Q^T (M=128 tokens, N=16
-//             heads, K=128 dims) into TMEM, then O^T[dim, head] = V^T . P^T
-//             (M=128 dims, N=2x16 heads, K=128 tokens) into TMEM, each issued
-//             as soon as its inputs are ready (no fixed QK/PV interleave).
+//   warp 7    tcgen05 issuer for S^T[tok, head] = K . Q^T (M=128 tokens,
+//             N=16 heads, K=128 dims) into TMEM;
+//   warp 1    tcgen05 issuer for O^T[dim, head] = V^T . P^T (M=128 dims,
+//             N=2x16 heads, K=128 tokens) into TMEM, and TMEM owner.
 //   warps 2-5 softmax + epilogue: thread = TMEM lane = token row for S and
 //             head-dim for O; fp32 online softmax in the log2 domain (the
 //             reference's convention, best :541-578), P written to shared
@@ -53,8 +53,14 @@ constexpr int kStageBytes = 2 * kOperandBytes + kQSlotBytes;  // K + V + Q: 68 K
 // side by side in the UMMA N dimension: 128 tokens x (2 x 16 heads) x 2 B.
 // Summing V.hi and V.lo keeps P's fp32 precision through a 16-bit MMA.
 constexpr int kPBufBytes = kTileTokens * 2 * kMaxGroup * 2;
-constexpr int kTmemCols = 128;                   // S0 S1 (16 cols each), O0 O1 (32 each)
-constexpr int kNumBars = 2 * kStages + 10;
+constexpr int kTmemCols = 128;                   // S0 S1 S2 (16 cols each), O0 O1 (32 each)
+// S^T tiles rotate through three TMEM buffers, P and O^T through two.  PV(i)
+// may overwrite O buffer i%2 once P(i) is written, since each softmax thread
+// loads O(i-2) before it writes P(i): the O buffers need no "empty" barrier.
+constexpr int kSBufs = 3;
+// kfull/kempty/vfull/vempty per stage, s_full/s_empty per S buffer, p_full/o_full x2
+constexpr int kNumBars = 4 * kStages + 2 * kSBufs + 4;
+constexpr int kQkWarp = 7;  // issues QK; warp 1 issues PV
 constexpr int kVProducerWarp = 6;
 
 // Shared-memory carve-up, offsets from a 1024-byte aligned base.
@@ -72,7 +78,8 @@ static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
 
 // TMEM columns: S^T of tile parity b at 16*b, O^T of tile parity b at 32+32*b.
 __device__ __forceinline__ uint32_t col_s(int b) { return static_cast<uint32_t>(b) * 16u; }
-__device__ __forceinline__ uint32_t col_o(int b) { return 32u + static_cast<uint32_t>(b) * 32u; }
+__device__ __forceinline__ uint32_t col_o(int b) { return 16u * kSBufs + static_cast<uint32_t>(b) * 32u; }
+static_assert(16 * kSBufs + 2 * 32 <= kTmemCols, "TMEM columns");
 
 // Arrival counter of a split (sequence, KV head) pair: bits [12, 32) hold the
 // launch epoch, bits [0, 12) the arrivals seen in that epoch.  A counter left
@@ -289,13 +296,16 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   uint8_t* stages = smem + kOffStages;
   uint8_t* pbufs = smem + kOffP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
-  uint64_t* full = bars;            // stage loaded: K, V and query rows (two producers)
-  uint64_t* empty = bars + kStages;  // stage consumed: P.V of its tile done
-  uint64_t* s_full = bars + 2 * kStages;
-  uint64_t* s_empty = s_full + 2;
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* o_full = p_full + 2;
-  uint64_t* o_empty = o_full + 2;
+  // The K ring (K tile + query rows) and the V ring share the stage slots
+  // but fill and drain independently: K is free once QK has run, V once P.V has.
+  uint64_t* kfull = bars;                 // [kStages] K + query rows landed
+  uint64_t* kempty = kfull + kStages;     // [kStages] QK of the tile done
+  uint64_t* vfull = kempty + kStages;     // [kStages] V landed
+  uint64_t* vempty = vfull + kStages;     // [kStages] P.V of the tile done
+  uint64_t* s_full = vempty + kStages;    // [kSBufs] S^T in TMEM
+  uint64_t* s_empty = s_full + kSBufs;    // [kSBufs] S^T read by the softmax warps
+  uint64_t* p_full = s_empty + kSBufs;    // [2] P written
+  uint64_t* o_full = p_full + 2;          // [2] O^T in TMEM
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
   volatile int* last_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 8);
@@ -318,17 +328,24 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   const int64_t max_len = p.bt_stride * static_cast<int64_t>(p.page);
 
   // ------------------------------------------------------------ prologue
+  // Nothing below reads global memory before pdl_wait_prerequisites(): the
+  // barrier set-up, TMEM allocation and shared-memory clearing may overlap
+  // the previous kernel on the stream when the launch allows it.
+  if (tid == 0) pdl_launch_dependents();
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 2);
-      mbar_init(&empty[s], 1);
+      mbar_init(&kfull[s], 1);
+      mbar_init(&kempty[s], 1);
+      mbar_init(&vfull[s], 1);
+      mbar_init(&vempty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kSBufs; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 128);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&p_full[i], 128);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 128);
     }
     *abort_flag = 0;
     *last_flag = 0;
@@ -347,10 +364,13 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     for (int i = tid; i < 2 * kPBufBytes / 16; i += kSm100Threads) z[i] = make_uint4(0, 0, 0, 0);
   }
   const CostModel cm{p.cost_tile, p.cost_seg};
+  pdl_wait_prerequisites();
   for (int b = tid; b < batch; b += kSm100Threads) {
-    int len = __ldg(p.seqlens + b);
-    len = len < 0 ? 0 : len;
-    len = static_cast<int>(len > max_len ? max_len : len);
+    const int stored = __ldg(p.seqlens + b);
+    // keys cached before this step plus the ones it appended
+    const int64_t want = static_cast<int64_t>(stored < 0 ? 0 : stored) + p.len_add;
+    const int64_t cap = max_len < 0x7fffffff ? max_len : 0x7fffffff;
+    const int len = static_cast<int>(want > cap ? cap : want);
     lens[b] = len;
     prefix[b + 1] = cm.pair_cost(len);
   }
@@ -413,8 +433,8 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         tma_prefetch_desc(&tm_k16);
       }
     }
-    uint64_t* ring_full = full;
-    uint64_t* ring_empty = empty;
+    uint64_t* ring_full = is_v ? vfull : kfull;
+    uint64_t* ring_empty = is_v ? vempty : kempty;
     const CUtensorMap* map_full = is_v ? &tm_v : &tm_k;
     const CUtensorMap* map_tail = is_v ? &tm_v16 : &tm_k16;
     const int operand_off = is_v ? kOperandBytes : 0;
@@ -467,88 +487,91 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       }
     }
     if (!is_v && lane == 0) *tiles_total = static_cast<int>(it);
-  } else if (warp == 1) {
-    // ---------------------------------------------------------- UMMA issuer
-    // Tiles 0 .. ntiles-1 of this CTA's range.  QK(i) needs stage i loaded
-    // and S buffer i%2 drained; PV(i) needs P(i) written and O buffer i%2
-    // drained.  Whichever is ready is issued (PV first: it frees a stage).
+  } else if (warp == 1 || warp == kQkWarp) {
+    // ---------------------------------------------------------- UMMA issuers
+    // A tcgen05.mma of M = 128, K = 16 occupies the tensor pipe ~48 cycles
+    // whatever N (up to 64), and the issuing thread stalls until it is taken,
+    // so one tile's 16 UMMAs keep an issuing thread busy for ~0.4 us.  Two
+    // warps issue: warp 7 runs QK(i) once K(i) has landed and S buffer i%3
+    // is drained; warp 1 runs P.V(i) once P(i) is written and V(i) has landed
+    // (P(i) also means O buffer i%2 is drained).  While one waits on its
+    // barriers the other's UMMAs keep the pipe busy.  Tiles 0 .. ntiles-1 of
+    // this CTA's range; the count is known once the producer has walked it.
+    const bool is_qk = warp == kQkWarp;
+    // Lane 0: wait for the phase; 1 = completed, 0 = tile idx does not exist
+    // (the range holds fewer tiles), -1 = gave up (timeout or abort).
+    auto issue_wait = [&](uint64_t* bar, uint32_t parity, int64_t idx) -> int {
+      uint64_t t0 = 0;
+      uint32_t spins = 0;
+      while (true) {
+        if (mbar_try_wait(bar, parity)) return 1;
+        if (idx >= *tiles_total) return 0;
+        if (((++spins) & 63u) == 0u) {
+          if (*abort_flag) return -1;
+          const uint64_t now = globaltimer_ns();
+          if (t0 == 0) {
+            t0 = now;
+          } else if (now - t0 > budget) {
+            *abort_flag = 1;
+            return -1;
+          }
+        }
+      }
+    };
     constexpr bool kBf16 = DType<T>::kBf16;
     constexpr uint32_t idesc_qk = make_idesc(kBf16, false, false, 128, kMaxGroup);
     constexpr uint32_t idesc_pv = make_idesc(kBf16, true, true, 128, kPvN);
-    int64_t qk = 0, pv = 0;
-    uint64_t idle_since = 0;
-    uint32_t spins = 0;
-    while (true) {
-      int action = 0;  // 1 = PV, 2 = QK, 3 = abort, 4 = all tiles done
+    for (int64_t i = 0;; ++i) {
+      int st = 1;
       if (lane == 0) {
-        const int64_t ntiles = *tiles_total;  // the producer's count once known
-        if (pv >= ntiles) action = 4;
-        if (action == 0 && pv < qk) {
-          const int pb = static_cast<int>(pv & 1);
-          const uint32_t ph = static_cast<uint32_t>((pv >> 1) & 1);
-          if (mbar_test_wait(&p_full[pb], ph) && mbar_test_wait(&o_empty[pb], ph ^ 1u)) action = 1;
-        }
-        if (action == 0 && qk < ntiles) {
-          const int st = static_cast<int>(qk % kStages);
-          if (mbar_test_wait(&full[st], static_cast<uint32_t>((qk / kStages) & 1)) &&
-              mbar_test_wait(&s_empty[qk & 1], static_cast<uint32_t>(((qk >> 1) & 1) ^ 1)))
-            action = 2;
-        }
-        if (action == 0) {
-          if (((++spins) & 255u) == 0u) {
-            const uint64_t now = globaltimer_ns();
-            if (idle_since == 0) idle_since = now;
-            if (*abort_flag || now - idle_since > budget) {
-              *abort_flag = 1;
-              action = 3;
+        const int stage = static_cast<int>(i % kStages);
+        const uint32_t ring_ph = static_cast<uint32_t>((i / kStages) & 1);
+        if (is_qk) {
+          const int sb = static_cast<int>(i % kSBufs);
+          st = issue_wait(&kfull[stage], ring_ph, i);
+          if (st == 1) st = issue_wait(&s_empty[sb], static_cast<uint32_t>(((i / kSBufs) & 1) ^ 1), i);
+          if (st == 1) {
+            tc_fence_after();
+            const uint32_t kaddr = smem_u32(stages + stage * kStageBytes);
+            const uint32_t qaddr = kaddr + 2 * kOperandBytes;
+#pragma unroll
+            for (int j = 0; j < kHeadDim / 16; ++j) {
+              // A = K tile, K-major 128B swizzle: 8-row groups 1 KB apart; the
+              // 16-dim step j moves 32 B inside a 128 B row, 64-dim halves 16 KB apart.
+              const uint64_t a =
+                  make_sdesc(kaddr + (j >> 2) * kHalfBytes + (j & 3) * 32, 16, 1024, kLayoutSw128);
+              const uint64_t b = make_sdesc(qaddr + (j >> 2) * (kQSlotBytes / 2) + (j & 3) * 32, 16,
+                                            1024, kLayoutSw128);
+              umma_f16(tmem + col_s(sb), a, b, idesc_qk, j > 0 ? 1u : 0u);
             }
+            umma_commit(&s_full[sb]);
+            umma_commit(&kempty[stage]);
           }
         } else {
-          idle_since = 0;
+          const int pb = static_cast<int>(i & 1);
+          st = issue_wait(&p_full[pb], static_cast<uint32_t>((i >> 1) & 1), i);
+          if (st == 1) st = issue_wait(&vfull[stage], ring_ph, i);
+          if (st == 1) {
+            tc_fence_after();
+            const uint32_t vaddr = smem_u32(stages + stage * kStageBytes + kOperandBytes);
+            const uint32_t paddr = smem_u32(pbufs + pb * kPBufBytes);
+#pragma unroll
+            for (int j = 0; j < kTileTokens / 16; ++j) {
+              // A = V^T: MN-major (head-dim contiguous), 128B swizzle; the two
+              // 64-dim halves are 16 KB apart (LBO), 8-token groups 1 KB apart (SBO).
+              const uint64_t a = make_sdesc(vaddr + j * 2048, kHalfBytes, 1024, kLayoutSw128);
+              // B = [P_hi | P_lo]^T: MN-major (heads contiguous), no swizzle;
+              // 8-column core matrices 128 B apart (SBO), 8-token groups kPGroupBytes apart (LBO).
+              const uint64_t b = make_sdesc(paddr + j * 2 * kPGroupBytes, kPGroupBytes, 128, kLayoutNone);
+              umma_f16(tmem + col_o(pb), a, b, idesc_pv, j > 0 ? 1u : 0u);
+            }
+            umma_commit(&o_full[pb]);
+            umma_commit(&vempty[stage]);
+          }
         }
       }
-      action = __shfl_sync(0xffffffffu, action, 0);
-      if (action >= 3) break;
-      if (action == 0) continue;
-      tc_fence_after();
-      if (lane == 0) {
-        if (action == 1) {
-          const int pb = static_cast<int>(pv & 1);
-          const int stage = static_cast<int>(pv % kStages);
-          const uint32_t vaddr = smem_u32(stages + stage * kStageBytes + kOperandBytes);
-          const uint32_t paddr = smem_u32(pbufs + pb * kPBufBytes);
-#pragma unroll
-          for (int j = 0; j < kTileTokens / 16; ++j) {
-            // A = V^T: MN-major (head-dim contiguous), 128B swizzle; the two
-            // 64-dim halves are 16 KB apart (LBO), 8-token groups 1 KB apart (SBO).
-            const uint64_t a = make_sdesc(vaddr + j * 2048, kHalfBytes, 1024, kLayoutSw128);
-            // B = [P_hi | P_lo]^T: MN-major (heads contiguous), no swizzle;
-            // 8-column core matrices 128 B apart (SBO), 8-token groups kPGroupBytes apart (LBO).
-            const uint64_t b = make_sdesc(paddr + j * 2 * kPGroupBytes, kPGroupBytes, 128, kLayoutNone);
-            umma_f16(tmem + col_o(pb), a, b, idesc_pv, j > 0 ? 1u : 0u);
-          }
-          umma_commit(&o_full[pb]);
-          umma_commit(&empty[stage]);
-        } else {
-          const int st = static_cast<int>(qk % kStages);
-          const int sb = static_cast<int>(qk & 1);
-          const uint32_t kaddr = smem_u32(stages + st * kStageBytes);
-          const uint32_t qaddr = kaddr + 2 * kOperandBytes;
-#pragma unroll
-          for (int j = 0; j < kHeadDim / 16; ++j) {
-            // A = K tile, K-major 128B swizzle: 8-row groups 1 KB apart; the
-            // 16-dim step j moves 32 B inside a 128 B row, 64-dim halves 16 KB apart.
-            const uint64_t a =
-                make_sdesc(kaddr + (j >> 2) * kHalfBytes + (j & 3) * 32, 16, 1024, kLayoutSw128);
-            const uint64_t b = make_sdesc(qaddr + (j >> 2) * (kQSlotBytes / 2) + (j & 3) * 32, 16,
-                                          1024, kLayoutSw128);
-            umma_f16(tmem + col_s(sb), a, b, idesc_qk, j > 0 ? 1u : 0u);
-          }
-          umma_commit(&s_full[sb]);
-        }
-      }
-      __syncwarp();
-      if (action == 1) ++pv; else ++qk;
+      st = __shfl_sync(0xffffffffu, st, 0);
+      if (st != 1) break;
     }
   } else {
     // ---------------------------------------------------------- softmax warps
@@ -584,8 +607,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       uint32_t r[kPvN];
       if constexpr (NCOL == 8) tmem_ld_x16(lane_addr + col_o(pb), r); else tmem_ld_x32(lane_addr + col_o(pb), r);
       tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&o_empty[pb]);
+      tc_fence_before();  // orders this load before the next P arrival (frees the O buffer)
 #pragma unroll
       for (int h = 0; h < NCOL; ++h) ov[h] = __uint_as_float(r[h]) + __uint_as_float(r[NCOL + h]);
     };
@@ -722,15 +744,21 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         prev_open = true;
       }
       // ---- softmax of tile `it`
-      const int sb = static_cast<int>(it & 1);
+      const int sb = static_cast<int>(it & 1);  // P buffer and max-exchange slot
       const int stage = static_cast<int>(it % kStages);
-      mbar_wait_bounded(&s_full[sb], static_cast<uint32_t>((it >> 1) & 1), abort_flag, budget);
+      {
+        const int sbuf = static_cast<int>(it % kSBufs);
+        mbar_wait_bounded(&s_full[sbuf], static_cast<uint32_t>((it / kSBufs) & 1), abort_flag, budget);
+      }
       tc_fence_after();
       uint32_t r[NCOL];
-      if constexpr (NCOL == 8) tmem_ld_x8(lane_addr + col_s(sb), r); else tmem_ld_x16(lane_addr + col_s(sb), r);
+      {
+        const uint32_t cs = col_s(static_cast<int>(it % kSBufs));
+        if constexpr (NCOL == 8) tmem_ld_x8(lane_addr + cs, r); else tmem_ld_x16(lane_addr + cs, r);
+      }
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(&s_empty[sb]);
+      mbar_arrive(&s_empty[it % kSBufs]);
 
       const int tok0 = (seg.tile0 + t) * kTileTokens;
       const int valid_rows = seg.seqlen - tok0;  // may exceed 128; <=0 only for empty sequences
@@ -758,9 +786,11 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         cur.l[h] = fmaf(cur.l[h], alpha[h], pv[h]);
         cur.m[h] = m_new;
       }
-      if (valid_rows < kTileTokens && !valid) {
+      if (valid_rows < kTileTokens && !valid &&
+          mbar_wait_bounded(&vfull[stage], static_cast<uint32_t>((it / kStages) & 1), abort_flag, budget)) {
         // Rows past the sequence end: stale or never-written data must not
-        // reach P.V (0 * NaN), so zero this token's V row in the stage.
+        // reach P.V (0 * NaN), so zero this token's V row in the stage, after
+        // the tile's V copy (whose last box may cover the row) has landed.
         uint4* vrow0 = reinterpret_cast<uint4*>(stages + stage * kStageBytes + kOperandBytes + row * 128);
         uint4* vrow1 = reinterpret_cast<uint4*>(stages + stage * kStageBytes + kOperandBytes + kHalfBytes + row * 128);
 #pragma unroll
@@ -857,8 +887,17 @@ cudaError_t launch_typed(const TensorMaps& m, const DecodeParams& p, int grid, c
     if (e != cudaSuccess) return e;
     __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
   }
-  kern<<<grid, kSm100Threads, kSmemBytes, stream>>>(m.q, m.k, m.v, m.k16, m.v16, p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kSm100Threads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, m.q, m.k, m.v, m.k16, m.v16, p);
 }
 
 template <typename T, typename OutT>

@@ -13,7 +13,7 @@ constexpr int kTileTokens = 128;       // KV tokens per pipeline stage (UMMA M o
 constexpr int kMaxGroup = 16;          // query heads per KV head (UMMA N, padded)
 constexpr int kMaxBatchPerLaunch = 512;   // sequences per launch (schedule lives in smem)
 constexpr int kMaxExchangeRanks = 8;   // GPUs of one node in a cross-GPU split-KV exchange
-constexpr int kSm100Threads = 224;     // warps 0/6 TMA, warp 1 MMA, warps 2-5 softmax/epilogue
+constexpr int kSm100Threads = 256;     // warps 0/6 TMA, warps 1/7 MMA (PV/QK), warps 2-5 softmax/epilogue
 
 // Per-launch parameters of the tensor-core kernel (tensor maps travel as
 // separate __grid_constant__ arguments).
@@ -43,6 +43,8 @@ struct DecodeParams {
   int64_t xlse_off;
   uint32_t xepoch;
   uint32_t* xdone;            // count of finished CTAs (workspace, zeroed before the launch)
+  int pdl;                    // launch with a programmatic dependency on the previous kernel
+  int len_add;                // keys appended this step: attended length = max(seqlens[b], 0) + len_add
   int cost_tile, cost_seg;    // split cost model: fixed cost per tile and per pair, in
                               // units where a full tile's K/V bytes cost 8
 };
@@ -56,7 +58,21 @@ struct SimtParams {
   int seqlen_q, causal;
   int64_t num_blocks;
   float scale_log2;
+  int len_add;  // as DecodeParams::len_add
 };
+
+// New keys/values written into the paged cache before attention
+// (flash_attn_with_kvcache's k / v arguments): row t of sequence b goes to
+// position max(seqlens[b], 0) + t.
+struct AppendParams {
+  const void* k_new; const void* v_new;  // [B, seqlen_new, Hkv, D]
+  void* k_cache; void* v_cache;          // [num_blocks, page, Hkv, D]
+  const int32_t* seqlens; const int32_t* block_table;
+  int64_t bt_stride, num_blocks;
+  int batch, seqlen_new, num_heads_k, head_dim, page, elem_bytes;
+  int* skipped;  // nullable: incremented per (b, t) row that had no page to go to
+};
+cudaError_t launch_append_kv(const AppendParams& p, cudaStream_t stream);
 
 // Workspace carve-up for the tensor-core kernel.
 struct WorkspaceLayout {

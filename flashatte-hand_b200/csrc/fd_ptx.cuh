@@ -86,6 +86,19 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: let a kernel launched after this one on the
+// stream start its prologue while this grid drains, and wait (before reading
+// anything an earlier kernel may have written) until the grid this one
+// depends on has completed and its writes are visible.  Both are no-ops
+// when the launch carries no programmatic dependency.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_prerequisites() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

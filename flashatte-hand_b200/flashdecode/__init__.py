@@ -5,8 +5,8 @@ Put the ``flashatte-hand_b200`` directory on ``sys.path`` and
 ``import flashdecode``.
 """
 from ._lib import FlashDecodeError, LIB_PATH, load_library
-from .ops import (combine_lse, device_status, flash_decode, last_error, run_kernel,
+from .ops import (append_kv, combine_lse, device_status, flash_decode, last_error, run_kernel,
                   workspace_size)
 
-__all__ = ["FlashDecodeError", "LIB_PATH", "load_library", "combine_lse", "device_status",
+__all__ = ["FlashDecodeError", "LIB_PATH", "load_library", "append_kv", "combine_lse", "device_status",
            "flash_decode", "last_error", "run_kernel", "workspace_size"]

@@ -27,6 +27,9 @@ SIGNATURES: dict[str, tuple] = {
     "fd_decode_paged_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp] + [_i64] * 7
                                 + [_i32, _i32, _f32, _i64, _vp]),
     "fd_decode_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
+    "fd_append_kv_paged": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp] + [_i64] * 7 + [_i32, _vp]),
+    "fd_decode_paged_kvappend": (_i32, [_vp] * 9 + [_i64] * 9 + [_i32, _i32, _f32, _i32, _i64, _vp,
+                                                                _sz, _vp]),
     "fd_combine_lse": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _vp, _vp]),
     "fd_xgpu_buffer_size": (_sz, [_i64, _i64, _i64, _i32]),
     "fd_xgpu_alloc": (_i32, [_sz, _c.POINTER(_vp), _c.c_char_p]),

@@ -69,16 +69,23 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                  out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
                  max_seqlen_k: int | None = None, workspace: torch.Tensor | None = None,
                  stream: torch.cuda.Stream | None = None, lse: torch.Tensor | None = None,
-                 causal: bool = False):
+                 causal: bool = False, k: torch.Tensor | None = None,
+                 v: torch.Tensor | None = None):
     """Paged decode attention for seqlen_q >= 1 query tokens per sequence.
 
     q [B, sq, Hq, D]; k_cache/v_cache [num_blocks, page, Hkv, D];
     cache_seqlens [B] int32; block_table [B, max_blocks] int32.
     Returns out [B, sq, Hq, D] (and lse fp32 natural log: [B, Hq] for sq = 1,
-    else [B, Hq, sq]).  causal: query token i sits at position
-    cache_seqlens[b] - sq + i and sees keys up to it.  `out` and `lse` may be
+    else [B, Hq, sq]).  causal: query token i sits at position L - sq + i
+    (L = attended keys) and sees keys up to it.  `out` and `lse` may be
     given as preallocated contiguous buffers; passing `lse` implies
     return_softmax_lse.
+
+    k / v [B, seqlen_new, Hkv, D] (optional, together): as in
+    flash_attn_with_kvcache, they are first written into the cache at
+    positions cache_seqlens[b] .. cache_seqlens[b] + seqlen_new - 1, then
+    attention runs over L = cache_seqlens[b] + seqlen_new keys;
+    cache_seqlens itself is left unchanged.
     """
     lib = load_library()
     _require_cuda(q, k_cache, v_cache, cache_seqlens, block_table)
@@ -115,6 +122,19 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     if workspace is not None:
         ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     st = stream if stream is not None else torch.cuda.current_stream(q.device)
+    if (k is None) != (v is None):
+        raise ValueError("k and v must be given together")
+    if k is not None:
+        _check_new_kv(k, v, k_cache, B)
+        with torch.cuda.device(q.device):
+            status = lib.fd_decode_paged_kvappend(
+                _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(k), _ptr(v), _ptr(out), _ptr(lse),
+                _ptr(cache_seqlens), _ptr(block_table), int(block_table.shape[1]), B, sq,
+                k.shape[1], Hq, Hkv, D, page, num_blocks, _DTYPES[q.dtype], _OUT_DTYPES[odt],
+                scale, 1 if causal else 0, int(max_seqlen_k or 0), ws_ptr, ws_bytes,
+                st.cuda_stream)
+        check(status)
+        return (out, lse) if return_softmax_lse else out
     with torch.cuda.device(q.device):
         status = lib.fd_decode_paged_mq(
             _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out), _ptr(lse), _ptr(cache_seqlens),
@@ -123,6 +143,43 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
             ws_ptr, ws_bytes, st.cuda_stream)
     check(status)
     return (out, lse) if return_softmax_lse else out
+
+
+def _check_new_kv(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, B: int) -> None:
+    _require_cuda(k, v)
+    if k.dim() != 4 or tuple(v.shape) != tuple(k.shape):
+        raise ValueError("k and v must both be [B, seqlen_new, Hkv, D]")
+    if k.shape[0] != B or k.shape[2] != k_cache.shape[2] or k.shape[3] != k_cache.shape[3]:
+        raise ValueError("k / v shape does not match the batch and cache heads")
+    if k.dtype != k_cache.dtype or v.dtype != k_cache.dtype:
+        raise ValueError("k / v must have the cache dtype")
+    if not (k.is_contiguous() and v.is_contiguous()):
+        raise ValueError("k and v must be contiguous")
+
+
+def append_kv(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+              cache_seqlens: torch.Tensor, block_table: torch.Tensor,
+              stream: torch.cuda.Stream | None = None) -> None:
+    """Write k / v [B, seqlen_new, Hkv, D] into the paged cache at positions
+    cache_seqlens[b] + t (the cache update of flash_attn_with_kvcache)."""
+    lib = load_library()
+    _require_cuda(k_cache, v_cache, cache_seqlens, block_table)
+    if cache_seqlens.dtype != torch.int32 or block_table.dtype != torch.int32:
+        raise ValueError("cache_seqlens and block_table must be int32")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous() and block_table.is_contiguous()):
+        raise ValueError("caches and block_table must be contiguous")
+    if k_cache.dtype not in _DTYPES or tuple(v_cache.shape) != tuple(k_cache.shape):
+        raise ValueError("k_cache/v_cache must be bf16 or fp16 with equal shapes")
+    B = block_table.shape[0]
+    _check_new_kv(k, v, k_cache, B)
+    num_blocks, page, Hkv, D = k_cache.shape
+    st = stream if stream is not None else torch.cuda.current_stream(k.device)
+    with torch.cuda.device(k.device):
+        status = lib.fd_append_kv_paged(
+            _ptr(k), _ptr(v), _ptr(k_cache), _ptr(v_cache), _ptr(cache_seqlens), _ptr(block_table),
+            int(block_table.shape[1]), B, k.shape[1], Hkv, D, page, num_blocks, _DTYPES[k.dtype],
+            st.cuda_stream)
+    check(status)
 
 
 def combine_lse(part_o: torch.Tensor, part_lse: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,
@@ -154,5 +211,5 @@ def combine_lse(part_o: torch.Tensor, part_lse: torch.Tensor, out_dtype: torch.d
     return (out, lse) if return_lse else out
 
 
-__all__ = ["run_kernel", "flash_decode", "combine_lse", "last_error", "device_status",
-           "workspace_size", "FlashDecodeError"]
+__all__ = ["run_kernel", "flash_decode", "append_kv", "combine_lse", "last_error",
+           "device_status", "workspace_size", "FlashDecodeError"]

@@ -115,6 +115,47 @@ size_t fd_decode_workspace_size_mq(int64_t batch_size, int64_t seqlen_q, int64_t
                                    int64_t num_heads_k, int64_t headdim);
 
 /*
+ * fd_append_kv_paged - write a step's new keys and values into the paged cache.
+ *
+ * Replaces: the cache update flash_attn_with_kvcache performs when given
+ * k / v (the reference evaluator passes None for both,
+ * scripts/evaluate_flashattn_submission.py:233-239, so no reference
+ * submission implements it).  k_new / v_new are [B, seqlen_new, Hkv, D];
+ * row t of sequence b is stored at position max(cache_seqlens[b], 0) + t,
+ * i.e. page block_table[b * block_table_stride + pos / page_block_size],
+ * row pos % page_block_size.  cache_seqlens is not modified (the caller
+ * advances it, as with flash_attn).  A row whose position lies past the
+ * block table, or whose page id is outside [0, num_blocks), is skipped.
+ */
+int fd_append_kv_paged(const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                       const int32_t* cache_seqlens, const int32_t* block_table,
+                       int64_t block_table_stride, int64_t batch_size, int64_t seqlen_new,
+                       int64_t num_heads_k, int64_t headdim, int64_t page_block_size,
+                       int64_t num_blocks, int dtype, void* stream);
+
+/*
+ * fd_decode_paged_kvappend - fd_append_kv_paged, then fd_decode_paged_mq over
+ * max(cache_seqlens[b], 0) + seqlen_new keys per sequence.
+ *
+ * Replaces: flash_attn_with_kvcache(q, k_cache, v_cache, k, v, cache_seqlens,
+ * block_table=..., causal=...) with k / v given, the call the reference
+ * evaluator makes with k = v = None (evaluate_flashattn_submission.py
+ * :232-247).  With causal, query token i sits at position
+ * max(cache_seqlens[b], 0) + seqlen_new - seqlen_q + i.  Arguments the
+ * attention half would reject are checked before the cache is written.
+ * max_seqlen_k bounds the attended length (cached + appended), 0 = unknown.
+ */
+int fd_decode_paged_kvappend(const void* q, void* k_cache, void* v_cache, const void* k_new,
+                             const void* v_new, void* out, float* lse,
+                             const int32_t* cache_seqlens, const int32_t* block_table,
+                             int64_t block_table_stride, int64_t batch_size, int64_t seqlen_q,
+                             int64_t seqlen_new, int64_t num_heads, int64_t num_heads_k,
+                             int64_t headdim, int64_t page_block_size, int64_t num_blocks,
+                             int dtype, int out_dtype, float softmax_scale, int causal,
+                             int64_t max_seqlen_k, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/*
  * fd_decode_paged_noalloc - fd_decode_paged for callers that cannot allocate
  * device memory: a process whose framework allocator already holds nearly
  * all of the GPU's memory (a library cudaMalloc would fail or fragment that

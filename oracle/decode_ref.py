@@ -109,6 +109,39 @@ def decode_reference_loops(q, k_cache, v_cache, cache_seqlens, block_table,
             torch.tensor(lse, dtype=torch.float64))
 
 
+def append_reference(k_cache: torch.Tensor, v_cache: torch.Tensor, k_new: torch.Tensor,
+                     v_new: torch.Tensor, cache_seqlens: torch.Tensor, block_table: torch.Tensor):
+    """Cache update of flash_attn_with_kvcache(k=k_new, v=v_new) on CPU copies.
+
+    Row t of sequence b goes to position max(L_b, 0) + t: page
+    block_table[b, pos // page], row pos % page (the same gather the reference
+    reads through, best :266-271).  A position past the table or a page id
+    outside the pool is skipped.  Returns (k_cache', v_cache', attended
+    lengths max(L_b, 0) + seqlen_new).  The reference evaluator passes
+    k = v = None (evaluate_flashattn_submission.py:233-239), so this restates
+    the documented flash_attn behaviour, pinned by tests/golden/ outputs.
+    """
+    kc = k_cache.cpu().clone()
+    vc = v_cache.cpu().clone()
+    kn, vn = k_new.cpu(), v_new.cpu()
+    B, sn = kn.shape[0], kn.shape[1]
+    nb, page = kc.shape[0], kc.shape[1]
+    bt = block_table.cpu()
+    stride = bt.shape[1]
+    lens = cache_seqlens.cpu().clamp(min=0)
+    for b in range(B):
+        for t in range(sn):
+            pos = int(lens[b]) + t
+            if pos // page >= stride:
+                continue
+            pg = int(bt[b, pos // page])
+            if pg < 0 or pg >= nb:
+                continue
+            kc[pg, pos % page] = kn[b, t]
+            vc[pg, pos % page] = vn[b, t]
+    return kc, vc, (lens + sn).to(torch.int32)
+
+
 def merge_partials(part_o: torch.Tensor, part_lse: torch.Tensor):
     """Merge normalised partials over disjoint KV ranges (natural-log LSE).
 

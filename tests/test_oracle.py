@@ -10,7 +10,8 @@ import pytest
 import torch
 
 from flashdecode import cases
-from oracle.decode_ref import decode_reference, decode_reference_loops, merge_partials
+from oracle.decode_ref import (append_reference, decode_reference, decode_reference_loops,
+                               merge_partials)
 
 GOLDEN_DIR = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -124,7 +125,28 @@ def test_oracle_matches_reference_oracle_golden(meta_file):
     with open(os.path.join(GOLDEN_DIR, meta_file)) as f:
         meta = json.load(f)
     data = np.load(os.path.join(GOLDEN_DIR, meta["npz"]))
-    from tests.golden.make_golden import build_case
+    from tests.golden.make_golden import build_append_case, build_case
+    if meta.get("kind") == "append":
+        # flash_attn_with_kvcache(k=, v=): append, then attend over L + sq keys
+        for spec in meta["cases"]:
+            c, t = build_append_case(spec)
+            kc, vc, lens = append_reference(t["k_cache"], t["v_cache"], t["k_new"], t["v_new"],
+                                            t["cache_seqlens"], t["block_table"])
+            o, l = decode_reference(t["q"], kc, vc, lens, t["block_table"],
+                                    softmax_scale=c.softmax_scale, causal=spec["causal"])
+            ref_o = torch.from_numpy(data[spec["name"] + "_out"]).float()
+            ref_l = torch.from_numpy(data[spec["name"] + "_lse"]).float()
+            if spec["sq"] == 1:
+                ref_l = ref_l[:, :, 0]
+            # flash_attn rounds P to bf16 (unit roundoff 2^-8) before P.V: on
+            # these short rows that error, bounded by 2^-8 * sum_t p_t |v_t|,
+            # is added to the north-star tolerance.
+            abs_o, _ = decode_reference(t["q"], kc, vc.abs(), lens, t["block_table"],
+                                        softmax_scale=c.softmax_scale, causal=spec["causal"])
+            allow = 2e-3 + 1e-2 * o.abs() + abs_o * 2.0 ** -8
+            assert bool(((o - ref_o).abs() <= allow).all()), spec["name"]
+            assert torch.allclose(l, ref_l, atol=1e-3), spec["name"]
+        return
     for spec in meta["cases"]:
         c, t = build_case(spec)
         o, l = decode_reference(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"], t["block_table"],
@@ -135,3 +157,48 @@ def test_oracle_matches_reference_oracle_golden(meta_file):
         # flash_attn output is rounded to the input dtype: rtol covers that rounding
         assert torch.allclose(o[valid], ref_o[valid], atol=2e-3, rtol=1e-2), spec["name"]
         assert torch.allclose(l[valid], ref_l[valid], atol=1e-3), spec["name"]
+
+
+def test_append_writes_rows_at_cached_length():
+    """Appended row t of sequence b lands at position L_b + t through the
+    page table (page crossing included); a one-hot appended key then takes
+    the whole softmax, so O equals its V row exactly."""
+    sn = 2
+    bt = torch.tensor([[0, 1, -1], [2, 3, -1], [4, 5, -1]], dtype=torch.int32)
+    kc = torch.zeros((6, 4, 1, 16))
+    vc = torch.randn((6, 4, 1, 16))
+    g = torch.Generator().manual_seed(3)
+    kn = torch.zeros((3, sn, 1, 16))
+    vn = torch.randn((3, sn, 1, 16), generator=g)
+    q = torch.zeros((3, 1, 2, 16))
+    q[:, 0, :, 5] = 1.0
+    kn[:, 1, 0, 5] = 60.0  # the last appended key dominates every score
+    seqlens = torch.tensor([3, 4, 0], dtype=torch.int32)
+    kc2, vc2, lens = append_reference(kc, vc, kn, vn, seqlens, bt)
+    assert lens.tolist() == [5, 6, 2]
+    # sequence 0: positions 3 (page 0 row 3) and 4 (page 1 row 0)
+    assert torch.equal(vc2[0, 3, 0], vn[0, 0, 0]) and torch.equal(vc2[1, 0, 0], vn[0, 1, 0])
+    assert torch.equal(vc2[3, 0, 0], vn[1, 0, 0]) and torch.equal(vc2[3, 1, 0], vn[1, 1, 0])
+    assert torch.equal(vc2[4, 0, 0], vn[2, 0, 0]) and torch.equal(vc2[4, 1, 0], vn[2, 1, 0])
+    untouched = torch.ones(6, 4, dtype=torch.bool)
+    for pg, r in [(0, 3), (1, 0), (3, 0), (3, 1), (4, 0), (4, 1)]:
+        untouched[pg, r] = False
+    assert torch.equal(vc2[untouched], vc[untouched])
+    o, _ = decode_reference(q, kc2, vc2, lens, bt, softmax_scale=1.0)
+    for b in range(3):
+        for h in range(2):
+            assert torch.equal(o[b, 0, h], vn[b, 1, 0])
+
+
+def test_append_skips_rows_without_a_page():
+    """Positions past the block table or on a page id outside the pool are
+    not written."""
+    kc = torch.zeros((2, 4, 1, 8))
+    vc = torch.zeros((2, 4, 1, 8))
+    kn = torch.ones((2, 3, 1, 8))
+    vn = torch.ones((2, 3, 1, 8))
+    bt = torch.tensor([[0], [7]], dtype=torch.int32)  # one page each; sequence 1's is out of the pool
+    kc2, vc2, lens = append_reference(kc, vc, kn, vn, torch.tensor([2, 0], dtype=torch.int32), bt)
+    assert lens.tolist() == [5, 3]
+    assert kc2[0, 2:].eq(1).all() and kc2[0, :2].eq(0).all()  # rows 2, 3 written; row 4 has no page
+    assert kc2[1].eq(0).all() and vc2[1].eq(0).all()
