@@ -130,8 +130,9 @@ CUresult encode(CUtensorMap* m, int dtype, int rank, const void* base, const cuu
                 const cuuint64_t* strides, const cuuint32_t* box) {
   const cuuint32_t estride[5] = {1, 1, 1, 1, 1};
   return encode_fn()(m,
-                     dtype == FD_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                     dtype == FD_DTYPE_E4M3   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                     : dtype == FD_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                      static_cast<cuuint32_t>(rank), const_cast<void*>(base), dims, strides, box,
                      estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -558,6 +559,8 @@ int fd_append_kv_paged(const void* k_new, const void* v_new, void* k_cache, void
   ap.num_heads_k = static_cast<int>(num_heads_k); ap.head_dim = static_cast<int>(headdim);
   ap.page = static_cast<int>(page_block_size); ap.elem_bytes = esize(dtype);
   ap.skipped = nullptr;
+  ap.k_scale = nullptr;
+  ap.v_scale = nullptr;
   const cudaError_t e = fd::launch_append_kv(ap, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "append launch: %s", cudaGetErrorString(e));
   return set_ok();
@@ -598,6 +601,255 @@ int fd_decode_paged_kvappend(const void* q, void* k_cache, void* v_cache, const 
                      num_blocks, dtype, out_dtype, softmax_scale, causal, max_seqlen_k,
                      static_cast<int>(seqlen_new), workspace, workspace_bytes, stream, nullptr,
                      nullptr);
+}
+
+// e4m3 K/V cache (see fd_decode_paged_fp8 in the header).  Per launch of at
+// most kMaxBatchPerLaunch sequences: split the query rows into e4m3 parts
+// (fd_qsplit.cu) into the workspace, then run the e4m3 tensor-core kernel.
+struct Kv8Layout {
+  fd::WorkspaceLayout base;
+  size_t q8_off, qinv_off, total;
+};
+static Kv8Layout kv8_layout(int64_t nb_max, int64_t num_heads_k, int64_t qrows, int sms) {
+  auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  Kv8Layout l;
+  l.base = fd::workspace_layout(nb_max, num_heads_k, qrows, sms);
+  const size_t pairs = static_cast<size_t>(nb_max * num_heads_k);
+  l.q8_off = up(l.base.total);
+  l.qinv_off = l.q8_off + up(pairs * 3 * fd::kMaxGroup * fd::kHeadDim);
+  l.total = l.qinv_off + up(pairs * fd::kMaxGroup * 4);
+  return l;
+}
+
+static int check_kv8_args(const void* q, const void* k_cache, const void* v_cache,
+                          const float* k_scale, const float* v_scale, const void* out,
+                          const int32_t* cache_seqlens, const int32_t* block_table,
+                          int64_t block_table_stride, int64_t batch_size, int64_t seqlen_q,
+                          int64_t num_heads, int64_t num_heads_k, int64_t headdim,
+                          int64_t page_block_size, int64_t num_blocks, int q_dtype, int out_dtype,
+                          float softmax_scale) {
+  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || k_scale == nullptr ||
+      v_scale == nullptr || out == nullptr || cache_seqlens == nullptr || block_table == nullptr)
+    return set_error(FD_ERR_INVALID_ARG, "null pointer");
+  if (batch_size <= 0 || seqlen_q <= 0 || num_heads <= 0 || num_heads_k <= 0 ||
+      page_block_size <= 0 || num_blocks <= 0 || block_table_stride <= 0)
+    return set_error(FD_ERR_INVALID_ARG, "sizes must be positive");
+  if (num_heads % num_heads_k != 0)
+    return set_error(FD_ERR_INVALID_ARG, "num_heads %lld not a multiple of num_heads_k %lld",
+                     (long long)num_heads, (long long)num_heads_k);
+  if (q_dtype != FD_DTYPE_BF16 && q_dtype != FD_DTYPE_FP16)
+    return set_error(FD_ERR_INVALID_ARG, "query dtype must be bf16 or fp16");
+  if (out_dtype != q_dtype && out_dtype != FD_DTYPE_FP32)
+    return set_error(FD_ERR_INVALID_ARG, "out_dtype must equal the query dtype or be fp32");
+  if (!std::isfinite(softmax_scale))
+    return set_error(FD_ERR_INVALID_ARG, "softmax_scale must be finite");
+  if (batch_size * seqlen_q * num_heads > INT32_MAX || seqlen_q > 65535 || num_blocks > INT32_MAX ||
+      page_block_size > INT32_MAX || num_heads > 65535)
+    return set_error(FD_ERR_UNSUPPORTED, "size exceeds 32-bit index range");
+  if (headdim != fd::kHeadDim)
+    return set_error(FD_ERR_UNSUPPORTED, "e4m3 cache: head dim must be 128 (got %lld)",
+                     (long long)headdim);
+  if (seqlen_q * (num_heads / num_heads_k) > fd::kMaxGroup)
+    return set_error(FD_ERR_UNSUPPORTED, "e4m3 cache: seqlen_q * group must be <= %d", fd::kMaxGroup);
+  if (pick_chunk(page_block_size) == 0)
+    return set_error(FD_ERR_UNSUPPORTED, "e4m3 cache: page size must be a multiple of 16");
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache))
+    return set_error(FD_ERR_UNSUPPORTED, "e4m3 cache: q/k/v must be 16-byte aligned");
+  if (encode_fn() == nullptr) return set_error(FD_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  return FD_OK;
+}
+
+static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cache,
+                           const float* k_scale, const float* v_scale, void* out, float* lse,
+                           const int32_t* cache_seqlens, const int32_t* block_table,
+                           int64_t block_table_stride, int64_t batch_size, int64_t seqlen_q,
+                           int64_t num_heads, int64_t num_heads_k, int64_t page_block_size,
+                           int64_t num_blocks, int q_dtype, int out_dtype, float softmax_scale,
+                           int causal, int64_t max_seqlen_k, int len_add, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices)
+    return set_error(FD_ERR_CUDA, "no current CUDA device");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int group = static_cast<int>(num_heads / num_heads_k);
+  const int64_t qrows = seqlen_q * group;
+  const int chunk = pick_chunk(page_block_size);
+  const int sms = device_sms(dev);
+  if (sms <= 0) return set_error(FD_ERR_CUDA, "cannot query SM count");
+  const int64_t nb_max = batch_size < fd::kMaxBatchPerLaunch ? batch_size : fd::kMaxBatchPerLaunch;
+  const Kv8Layout wl = kv8_layout(nb_max, num_heads_k, qrows, sms);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (ws == nullptr) {
+    ws = static_cast<uint8_t*>(internal_workspace(dev, wl.total, st));
+    if (ws == nullptr) return set_error(FD_ERR_WORKSPACE, "cannot allocate %zu-byte workspace", wl.total);
+  } else if (workspace_bytes < wl.total) {
+    return set_error(FD_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, wl.total);
+  } else if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) {
+    return set_error(FD_ERR_WORKSPACE, "workspace not 256-byte aligned");
+  }
+  const int64_t kv_max = block_table_stride * page_block_size;
+  const int64_t len_bound =
+      max_seqlen_k > 0 ? (max_seqlen_k < kv_max ? max_seqlen_k : kv_max) : kv_max;
+  const int64_t tiles_bound = len_bound > 0 ? (len_bound + fd::kTileTokens - 1) / fd::kTileTokens : 1;
+  fd::TensorMaps maps;
+  {
+    // e4m3 rows: one 128-byte row per (token, KV head)
+    const cuuint64_t dims[4] = {128, (cuuint64_t)num_heads_k, (cuuint64_t)page_block_size,
+                                (cuuint64_t)num_blocks};
+    const cuuint64_t strides[3] = {128, (cuuint64_t)(num_heads_k * 128),
+                                   (cuuint64_t)(page_block_size * num_heads_k * 128)};
+    const cuuint32_t box[4] = {128, 1, (cuuint32_t)chunk, 1};
+    const cuuint32_t box16[4] = {128, 1, 16, 1};
+    CUresult r = encode(&maps.k, FD_DTYPE_E4M3, 4, k_cache, dims, strides, box);
+    if (r == CUDA_SUCCESS) r = encode(&maps.v, FD_DTYPE_E4M3, 4, v_cache, dims, strides, box);
+    if (r == CUDA_SUCCESS) r = encode(&maps.k16, FD_DTYPE_E4M3, 4, k_cache, dims, strides, box16);
+    if (r == CUDA_SUCCESS) r = encode(&maps.v16, FD_DTYPE_E4M3, 4, v_cache, dims, strides, box16);
+    if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "K/V tensor map encode failed (%d)", (int)r);
+  }
+  const int64_t per_seq_cost =
+      cost_seg() + ((kv_max + fd::kTileTokens - 1) / fd::kTileTokens + 1) *
+                       (8 + static_cast<int64_t>(cost_tile()));
+  if (per_seq_cost > INT32_MAX) return set_error(FD_ERR_UNSUPPORTED, "sequence too long");
+  int64_t per_launch = INT32_MAX / per_seq_cost;
+  if (per_launch > fd::kMaxBatchPerLaunch) per_launch = fd::kMaxBatchPerLaunch;
+  const int es = esize(q_dtype);
+  uint8_t* q8 = ws + wl.q8_off;
+  float* q_inv = reinterpret_cast<float*>(ws + wl.qinv_off);
+  for (int64_t b0 = 0; b0 < batch_size; b0 += per_launch) {
+    const int64_t nb = batch_size - b0 < per_launch ? batch_size - b0 : per_launch;
+    const uint8_t* qb = static_cast<const uint8_t*>(q) + b0 * seqlen_q * num_heads * 128 * es;
+    cudaError_t e = fd::launch_split_query(qb, q_dtype, static_cast<int>(nb),
+                                           static_cast<int>(seqlen_q), static_cast<int>(num_heads),
+                                           static_cast<int>(num_heads_k), q8, q_inv, st);
+    if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "query split launch: %s", cudaGetErrorString(e));
+    {
+      // [nb * Hkv] blocks of 48 rows x 128 bytes, one box per (sequence, KV head)
+      const cuuint64_t dims[3] = {128, 3 * fd::kMaxGroup, (cuuint64_t)(nb * num_heads_k)};
+      const cuuint64_t strides[2] = {128, 3 * fd::kMaxGroup * 128};
+      const cuuint32_t box[3] = {128, 3 * fd::kMaxGroup, 1};
+      const CUresult r = encode(&maps.q, FD_DTYPE_E4M3, 3, q8, dims, strides, box);
+      if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "query-part tensor map encode failed (%d)", (int)r);
+    }
+    fd::DecodeParams p{};
+    p.out = static_cast<uint8_t*>(out) + b0 * seqlen_q * num_heads * 128 * esize(out_dtype);
+    p.lse = lse != nullptr ? lse + b0 * num_heads * seqlen_q : nullptr;
+    p.seqlens = cache_seqlens + b0;
+    p.block_table = block_table + b0 * block_table_stride;
+    p.bt_stride = block_table_stride;
+    p.batch = static_cast<int>(nb);
+    p.num_heads = static_cast<int>(num_heads);
+    p.num_heads_k = static_cast<int>(num_heads_k);
+    p.group = group;
+    p.seqlen_q = static_cast<int>(seqlen_q);
+    p.causal = causal ? 1 : 0;
+    p.qrows = static_cast<int>(qrows);
+    p.page = static_cast<int>(page_block_size);
+    p.chunk = chunk;
+    p.scale_log2 = softmax_scale * 1.4426950408889634f;
+    p.err = reinterpret_cast<int*>(ws + wl.base.err_off);
+    p.tickets = reinterpret_cast<uint32_t*>(ws + wl.base.tickets_off);
+    p.part_lse = reinterpret_cast<float*>(ws + wl.base.lse_off);
+    p.part_o = reinterpret_cast<float*>(ws + wl.base.o_off);
+    p.timeout_ns = timeout_ns();
+    p.epoch = next_epoch();
+    p.cost_tile = cost_tile();
+    p.cost_seg = cost_seg();
+    p.xworld = 0;
+    p.pdl = pdl_enabled() ? 1 : 0;
+    p.len_add = len_add;
+    p.k_scale = k_scale;
+    p.v_scale = v_scale;
+    p.q_inv = q_inv;
+    const int64_t work_bound = nb * num_heads_k * tiles_bound;
+    const int grid = static_cast<int>(work_bound < sms ? work_bound : sms);
+    e = fd::launch_decode_sm100_kv8(maps, p, q_dtype, out_dtype == FD_DTYPE_FP32, grid, st);
+    if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "sm100 e4m3 launch: %s", cudaGetErrorString(e));
+  }
+  return set_ok();
+}
+
+size_t fd_decode_workspace_size_fp8(int64_t batch_size, int64_t seqlen_q, int64_t num_heads,
+                                    int64_t num_heads_k, int64_t headdim) {
+  if (batch_size <= 0 || seqlen_q <= 0 || num_heads <= 0 || num_heads_k <= 0 ||
+      num_heads % num_heads_k != 0 || headdim != fd::kHeadDim)
+    return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices) return 0;
+  const int sms = device_sms(dev);
+  if (sms <= 0) return 0;
+  const int64_t nb = batch_size < fd::kMaxBatchPerLaunch ? batch_size : fd::kMaxBatchPerLaunch;
+  return kv8_layout(nb, num_heads_k, seqlen_q * (num_heads / num_heads_k), sms).total;
+}
+
+int fd_append_kv_paged_fp8(const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                           const float* k_scale, const float* v_scale,
+                           const int32_t* cache_seqlens, const int32_t* block_table,
+                           int64_t block_table_stride, int64_t batch_size, int64_t seqlen_new,
+                           int64_t num_heads_k, int64_t headdim, int64_t page_block_size,
+                           int64_t num_blocks, int src_dtype, void* stream) {
+  if (k_new == nullptr || v_new == nullptr || k_cache == nullptr || v_cache == nullptr ||
+      k_scale == nullptr || v_scale == nullptr || cache_seqlens == nullptr || block_table == nullptr)
+    return set_error(FD_ERR_INVALID_ARG, "null pointer");
+  if (batch_size <= 0 || seqlen_new <= 0 || num_heads_k <= 0 || headdim <= 0 ||
+      page_block_size <= 0 || num_blocks <= 0 || block_table_stride <= 0)
+    return set_error(FD_ERR_INVALID_ARG, "sizes must be positive");
+  if (src_dtype != FD_DTYPE_BF16 && src_dtype != FD_DTYPE_FP16)
+    return set_error(FD_ERR_INVALID_ARG, "new rows must be bf16 or fp16");
+  if (headdim % 8 != 0 || (reinterpret_cast<uintptr_t>(k_cache) & 7u) != 0 ||
+      (reinterpret_cast<uintptr_t>(v_cache) & 7u) != 0)
+    return set_error(FD_ERR_UNSUPPORTED, "e4m3 append: head dim must be a multiple of 8, caches 8-byte aligned");
+  if (seqlen_new > 65535 || batch_size * seqlen_new > INT32_MAX || page_block_size > INT32_MAX ||
+      num_heads_k * headdim > INT32_MAX)
+    return set_error(FD_ERR_UNSUPPORTED, "size exceeds 32-bit index range");
+  fd::AppendParams ap;
+  ap.k_new = k_new; ap.v_new = v_new; ap.k_cache = k_cache; ap.v_cache = v_cache;
+  ap.seqlens = cache_seqlens; ap.block_table = block_table;
+  ap.bt_stride = block_table_stride; ap.num_blocks = num_blocks;
+  ap.batch = static_cast<int>(batch_size); ap.seqlen_new = static_cast<int>(seqlen_new);
+  ap.num_heads_k = static_cast<int>(num_heads_k); ap.head_dim = static_cast<int>(headdim);
+  ap.page = static_cast<int>(page_block_size); ap.elem_bytes = 1;
+  ap.skipped = nullptr;
+  ap.k_scale = k_scale;
+  ap.v_scale = v_scale;
+  const cudaError_t e = fd::launch_append_kv_e4m3(ap, src_dtype, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "e4m3 append launch: %s", cudaGetErrorString(e));
+  return set_ok();
+}
+
+int fd_decode_paged_fp8(const void* q, void* k_cache, void* v_cache, const float* k_scale,
+                        const float* v_scale, const void* k_new, const void* v_new,
+                        int64_t seqlen_new, void* out, float* lse, const int32_t* cache_seqlens,
+                        const int32_t* block_table, int64_t block_table_stride,
+                        int64_t batch_size, int64_t seqlen_q, int64_t num_heads,
+                        int64_t num_heads_k, int64_t headdim, int64_t page_block_size,
+                        int64_t num_blocks, int q_dtype, int out_dtype, float softmax_scale,
+                        int causal, int64_t max_seqlen_k, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  int st = check_kv8_args(q, k_cache, v_cache, k_scale, v_scale, out, cache_seqlens, block_table,
+                          block_table_stride, batch_size, seqlen_q, num_heads, num_heads_k,
+                          headdim, page_block_size, num_blocks, q_dtype, out_dtype, softmax_scale);
+  if (st != FD_OK) return st;
+  if ((k_new == nullptr) != (v_new == nullptr))
+    return set_error(FD_ERR_INVALID_ARG, "k_new and v_new must be given together");
+  int len_add = 0;
+  if (k_new != nullptr) {
+    if (seqlen_new <= 0 || seqlen_new > 65535)
+      return set_error(FD_ERR_INVALID_ARG, "seqlen_new out of range");
+    if (workspace != nullptr &&
+        workspace_bytes < fd_decode_workspace_size_fp8(batch_size, seqlen_q, num_heads, num_heads_k,
+                                                       headdim))
+      return set_error(FD_ERR_WORKSPACE, "workspace too small");
+    st = fd_append_kv_paged_fp8(k_new, v_new, k_cache, v_cache, k_scale, v_scale, cache_seqlens,
+                                block_table, block_table_stride, batch_size, seqlen_new,
+                                num_heads_k, headdim, page_block_size, num_blocks, q_dtype, stream);
+    if (st != FD_OK) return st;
+    len_add = static_cast<int>(seqlen_new);
+  }
+  return decode_kv8_impl(q, k_cache, v_cache, k_scale, v_scale, out, lse, cache_seqlens,
+                         block_table, block_table_stride, batch_size, seqlen_q, num_heads,
+                         num_heads_k, page_block_size, num_blocks, q_dtype, out_dtype,
+                         softmax_scale, causal, max_seqlen_k, len_add, workspace, workspace_bytes,
+                         stream);
 }
 
 int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, void* out, float* lse,

@@ -38,48 +38,60 @@
 #include <type_traits>
 
 #include "fd_kernels.h"
+#include "fd_fp8.cuh"
 #include "fd_ptx.cuh"
 
 namespace fd {
 
 namespace {
 
-constexpr int kStages = 3;
-constexpr int kHalfBytes = kTileTokens * 128;    // 128 tokens x 64 dims x 2 B = 16 KB
-constexpr int kOperandBytes = 2 * kHalfBytes;    // one K or V tile: 32 KB
-constexpr int kQSlotBytes = 2 * kMaxGroup * 128; // two halves x 16 rows x 128 B
-constexpr int kStageBytes = 2 * kOperandBytes + kQSlotBytes;  // K + V + Q: 68 KB
-// P is stored as two 16-bit parts, P = hi + lo (hi = round(P), lo = round(P - hi)),
-// side by side in the UMMA N dimension: 128 tokens x (2 x 16 heads) x 2 B.
-// Summing V.hi and V.lo keeps P's fp32 precision through a 16-bit MMA.
-constexpr int kPBufBytes = kTileTokens * 2 * kMaxGroup * 2;
-constexpr int kTmemCols = 128;                   // S0 S1 S2 (16 cols each), O0 O1 (32 each)
+// Stage / buffer geometry, by K/V element type.
+//   16-bit K/V: a 128-token K or V tile is two 64-dim halves of 128 B rows
+//   (16 KB each, 128B-swizzled); the group's query rows ride in each stage;
+//   P is two 16-bit parts (hi = round(P), lo = round(P - hi)) side by side in
+//   the UMMA N dimension, so summing V.hi and V.lo keeps P's fp32 precision.
+//   e4m3 K/V: one 128 B row holds all 128 dims, a tile is 16 KB; the query
+//   rows arrive pre-split into three e4m3 parts (48 rows of 128 B) and P is
+//   split into three e4m3 parts the same way (see the softmax warps).
 // S^T tiles rotate through three TMEM buffers, P and O^T through two.  PV(i)
 // may overwrite O buffer i%2 once P(i) is written, since each softmax thread
 // loads O(i-2) before it writes P(i): the O buffers need no "empty" barrier.
-constexpr int kSBufs = 3;
-// kfull/kempty/vfull/vempty per stage, s_full/s_empty per S buffer, p_full/o_full x2
-constexpr int kNumBars = 4 * kStages + 2 * kSBufs + 4;
+template <bool KV8> struct Geo {
+  static constexpr int kStages = KV8 ? 5 : 3;
+  static constexpr int kHalfBytes = kTileTokens * 128;              // 128 rows x 128 B
+  static constexpr int kOperandBytes = KV8 ? kHalfBytes : 2 * kHalfBytes;  // one K or V tile
+  static constexpr int kParts = KV8 ? 3 : 2;                        // P (and Q) parts
+  static constexpr int kQSlotBytes = KV8 ? 3 * kMaxGroup * 128 : 2 * kMaxGroup * 128;
+  static constexpr int kStageBytes = 2 * kOperandBytes + kQSlotBytes;
+  static constexpr int kPBufBytes = KV8 ? kTileTokens * 3 * kMaxGroup : kTileTokens * 2 * kMaxGroup * 2;
+  static constexpr int kSCols = KV8 ? 3 * kMaxGroup : kMaxGroup;    // TMEM columns of one S^T tile
+  static constexpr int kOCols = KV8 ? 3 * kMaxGroup : 2 * kMaxGroup;  // of one O^T tile
+  static constexpr int kSBufs = 3;
+  static constexpr int kTmemCols = KV8 ? 256 : 128;
+  // kfull/kempty/vfull/vempty per stage, s_full/s_empty per S buffer, p_full/o_full x2
+  static constexpr int kNumBars = 4 * kStages + 2 * kSBufs + 4;
+  // Shared-memory carve-up, offsets from a 1024-byte aligned base.
+  static constexpr int kOffStages = 0;
+  static constexpr int kOffP = kOffStages + kStages * kStageBytes;
+  static constexpr int kOffBars = kOffP + 2 * kPBufBytes;
+  static constexpr int kOffMisc = kOffBars + kNumBars * 8;           // tmem slot, abort, last flag
+  static constexpr int kOffRed = (kOffMisc + 64 + 15) & ~15;         // [2][4][16] floats tile maxima
+  static constexpr int kOffFin = kOffRed + 2 * 4 * kMaxGroup * 4;    // [2][4][16] floats row sums
+  static constexpr int kOffPrefix = kOffFin + 2 * 4 * kMaxGroup * 4; // [B+1] pair-cost prefix sums
+  static constexpr int kOffLens = kOffPrefix + (kMaxBatchPerLaunch + 1) * 4;  // [B] clamped lengths
+  static constexpr int kSmemUsed = kOffLens + kMaxBatchPerLaunch * 4;
+  static constexpr int kSmemBytes = kSmemUsed + 1024;                // slack for 1024-B alignment
+  static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
+  static_assert(kStageBytes % 1024 == 0 && kOffP % 1024 == 0, "swizzled tiles need 1 KB alignment");
+  static_assert(kSBufs * kSCols + 2 * kOCols <= kTmemCols, "TMEM columns");
+  // TMEM columns: S^T buffer b at kSCols * b, O^T buffer b after the S buffers.
+  static __device__ __forceinline__ uint32_t col_s(int b) { return static_cast<uint32_t>(b * kSCols); }
+  static __device__ __forceinline__ uint32_t col_o(int b) {
+    return static_cast<uint32_t>(kSBufs * kSCols + b * kOCols);
+  }
+};
 constexpr int kQkWarp = 7;  // issues QK; warp 1 issues PV
 constexpr int kVProducerWarp = 6;
-
-// Shared-memory carve-up, offsets from a 1024-byte aligned base.
-constexpr int kOffStages = 0;
-constexpr int kOffP = kOffStages + kStages * kStageBytes;
-constexpr int kOffBars = kOffP + 2 * kPBufBytes;
-constexpr int kOffMisc = kOffBars + kNumBars * 8;            // tmem slot, abort, last flag
-constexpr int kOffRed = (kOffMisc + 64 + 15) & ~15;          // [2][4][16] floats tile maxima
-constexpr int kOffFin = kOffRed + 2 * 4 * kMaxGroup * 4;     // [2][4][16] floats row sums
-constexpr int kOffPrefix = kOffFin + 2 * 4 * kMaxGroup * 4;  // [B+1] ints pair-cost prefix sums
-constexpr int kOffLens = kOffPrefix + (kMaxBatchPerLaunch + 1) * 4;  // [B] ints clamped lengths
-constexpr int kSmemUsed = kOffLens + kMaxBatchPerLaunch * 4;
-constexpr int kSmemBytes = kSmemUsed + 1024;                 // slack for 1024-B alignment
-static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
-
-// TMEM columns: S^T of tile parity b at 16*b, O^T of tile parity b at 32+32*b.
-__device__ __forceinline__ uint32_t col_s(int b) { return static_cast<uint32_t>(b) * 16u; }
-__device__ __forceinline__ uint32_t col_o(int b) { return 16u * kSBufs + static_cast<uint32_t>(b) * 32u; }
-static_assert(16 * kSBufs + 2 * 32 <= kTmemCols, "TMEM columns");
 
 // Arrival counter of a split (sequence, KV head) pair: bits [12, 32) hold the
 // launch epoch, bits [0, 12) the arrivals seen in that epoch.  A counter left
@@ -116,6 +128,14 @@ __host__ __device__ constexpr uint32_t make_idesc(bool bf16, bool a_mn_major, bo
                                                   int m, int n) {
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
          ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// UMMA instruction descriptor for kind::f8f6f4, both operands e4m3 (format
+// code 0), fp32 accumulator.
+__host__ __device__ constexpr uint32_t make_idesc_e4m3(bool a_mn_major, bool b_mn_major, int m,
+                                                       int n) {
+  return (1u << 4) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
@@ -278,43 +298,45 @@ __device__ __forceinline__ bool lane0_wait(uint64_t* bar, uint32_t parity, volat
 
 // MULTI = false: one query token per sequence, no causal mask (plain decode).
 // MULTI = true: seqlen_q query tokens, optional bottom-right causal mask.
-template <typename T, typename OutT, int NCOL, bool MULTI, bool XCHG>
+template <typename T, typename OutT, int NCOL, bool MULTI, bool XCHG, bool KV8>
 __global__ void __launch_bounds__(kSm100Threads, 1)
     decode_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v,
                         const __grid_constant__ CUtensorMap tm_k16,
                         const __grid_constant__ CUtensorMap tm_v16, const DecodeParams p) {
+  using G = Geo<KV8>;
   // P.V uses N = 2*NCOL columns: NCOL hi parts then NCOL lo parts of P.
   constexpr int kPvN = 2 * NCOL;
   constexpr int kPGroupBytes = (kPvN / 8) * 128;  // one 8-token group of P rows
+  constexpr int kPGroupBytes8 = 3 * 128;           // the same for the three e4m3 parts of P
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
 
   // Stage s: K tile at +0, V tile at +32 KB, query rows at +64 KB.
-  uint8_t* stages = smem + kOffStages;
-  uint8_t* pbufs = smem + kOffP;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
+  uint8_t* stages = smem + G::kOffStages;
+  uint8_t* pbufs = smem + G::kOffP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::kOffBars);
   // The K ring (K tile + query rows) and the V ring share the stage slots
   // but fill and drain independently: K is free once QK has run, V once P.V has.
-  uint64_t* kfull = bars;                 // [kStages] K + query rows landed
-  uint64_t* kempty = kfull + kStages;     // [kStages] QK of the tile done
-  uint64_t* vfull = kempty + kStages;     // [kStages] V landed
-  uint64_t* vempty = vfull + kStages;     // [kStages] P.V of the tile done
-  uint64_t* s_full = vempty + kStages;    // [kSBufs] S^T in TMEM
-  uint64_t* s_empty = s_full + kSBufs;    // [kSBufs] S^T read by the softmax warps
-  uint64_t* p_full = s_empty + kSBufs;    // [2] P written
+  uint64_t* kfull = bars;                 // [G::kStages] K + query rows landed
+  uint64_t* kempty = kfull + G::kStages;     // [G::kStages] QK of the tile done
+  uint64_t* vfull = kempty + G::kStages;     // [G::kStages] V landed
+  uint64_t* vempty = vfull + G::kStages;     // [G::kStages] P.V of the tile done
+  uint64_t* s_full = vempty + G::kStages;    // [G::kSBufs] S^T in TMEM
+  uint64_t* s_empty = s_full + G::kSBufs;    // [G::kSBufs] S^T read by the softmax warps
+  uint64_t* p_full = s_empty + G::kSBufs;    // [2] P written
   uint64_t* o_full = p_full + 2;          // [2] O^T in TMEM
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
-  volatile int* last_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 8);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + G::kOffMisc + 4);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(smem + G::kOffMisc + 8);
   // Tiles of this CTA, published by the producer once its walk is done.
-  volatile int* tiles_total = reinterpret_cast<volatile int*>(smem + kOffMisc + 12);
-  float* red = reinterpret_cast<float*>(smem + kOffRed);
-  float* fin = reinterpret_cast<float*>(smem + kOffFin);
-  int* prefix = reinterpret_cast<int*>(smem + kOffPrefix);
-  int* lens = reinterpret_cast<int*>(smem + kOffLens);
+  volatile int* tiles_total = reinterpret_cast<volatile int*>(smem + G::kOffMisc + 12);
+  float* red = reinterpret_cast<float*>(smem + G::kOffRed);
+  float* fin = reinterpret_cast<float*>(smem + G::kOffFin);
+  int* prefix = reinterpret_cast<int*>(smem + G::kOffPrefix);
+  int* lens = reinterpret_cast<int*>(smem + G::kOffLens);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -333,13 +355,13 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   // the previous kernel on the stream when the launch allows it.
   if (tid == 0) pdl_launch_dependents();
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < G::kStages; ++s) {
       mbar_init(&kfull[s], 1);
       mbar_init(&kempty[s], 1);
       mbar_init(&vfull[s], 1);
       mbar_init(&vempty[s], 1);
     }
-    for (int i = 0; i < kSBufs; ++i) {
+    for (int i = 0; i < G::kSBufs; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 128);
     }
@@ -352,16 +374,16 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     *tiles_total = 0x7fffffff;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == 1) tmem_alloc(tmem_slot, G::kTmemCols);
   // Zero the stages' query areas (rows >= qrows stay zero: the query TMA
   // writes rows < qrows only) and the P buffers (columns >= qrows stay zero).
-  for (int s = 0; s < kStages; ++s) {
-    uint4* z = reinterpret_cast<uint4*>(stages + s * kStageBytes + 2 * kOperandBytes);
-    for (int i = tid; i < kQSlotBytes / 16; i += kSm100Threads) z[i] = make_uint4(0, 0, 0, 0);
+  for (int s = 0; s < G::kStages; ++s) {
+    uint4* z = reinterpret_cast<uint4*>(stages + s * G::kStageBytes + 2 * G::kOperandBytes);
+    for (int i = tid; i < G::kQSlotBytes / 16; i += kSm100Threads) z[i] = make_uint4(0, 0, 0, 0);
   }
   {
     uint4* z = reinterpret_cast<uint4*>(pbufs);
-    for (int i = tid; i < 2 * kPBufBytes / 16; i += kSm100Threads) z[i] = make_uint4(0, 0, 0, 0);
+    for (int i = tid; i < 2 * G::kPBufBytes / 16; i += kSm100Threads) z[i] = make_uint4(0, 0, 0, 0);
   }
   const CostModel cm{p.cost_tile, p.cost_seg};
   pdl_wait_prerequisites();
@@ -437,8 +459,11 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     uint64_t* ring_empty = is_v ? vempty : kempty;
     const CUtensorMap* map_full = is_v ? &tm_v : &tm_k;
     const CUtensorMap* map_tail = is_v ? &tm_v16 : &tm_k16;
-    const int operand_off = is_v ? kOperandBytes : 0;
-    const uint32_t extra_tx = is_v ? 0u : 2u * qrows * 128u;  // query rows ride with K
+    const int operand_off = is_v ? G::kOperandBytes : 0;
+    // query rows ride with K: 16-bit rows (two halves of qrows x 128 B), or
+    // the 48 x 128 B block of e4m3 query parts
+    const uint32_t extra_tx = is_v ? 0u : (KV8 ? static_cast<uint32_t>(G::kQSlotBytes) : 2u * qrows * 128u);
+    constexpr uint32_t kRowTx = KV8 ? 128u : 256u;  // K or V bytes per token
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_keep = policy_evict_last();
     const int chunk = p.chunk;  // tokens per TMA box of a full tile; never crosses a page
@@ -460,19 +485,23 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         const bool need = lane < nbox;
         int page_id = 0;
         if (need) page_id = __ldg(bt_row + pos / p.page);  // issued before the wait
-        const int stage = static_cast<int>(it % kStages);
-        ok = lane0_wait(&ring_empty[stage], static_cast<uint32_t>((it / kStages) & 1) ^ 1u,
+        const int stage = static_cast<int>(it % G::kStages);
+        ok = lane0_wait(&ring_empty[stage], static_cast<uint32_t>((it / G::kStages) & 1) ^ 1u,
                         abort_flag, budget, lane);
         if (!ok) break;
-        uint8_t* sdst = stages + stage * kStageBytes;
+        uint8_t* sdst = stages + stage * G::kStageBytes;
         if (lane == 0) {
-          mbar_arrive_expect_tx(&ring_full[stage], static_cast<uint32_t>(nbox * box) * 256u + extra_tx);
+          mbar_arrive_expect_tx(&ring_full[stage], static_cast<uint32_t>(nbox * box) * kRowTx + extra_tx);
           if (!is_v) {
-            uint8_t* qdst = sdst + 2 * kOperandBytes;
-            // rows qi * group + g: query token qi, head kvh * group + g
-            tma_load_4d(&tm_q, &ring_full[stage], qdst, 0, s.kvh * group, 0, s.b, pol_keep);
-            tma_load_4d(&tm_q, &ring_full[stage], qdst + kQSlotBytes / 2, 64, s.kvh * group, 0, s.b,
-                        pol_keep);
+            uint8_t* qdst = sdst + 2 * G::kOperandBytes;
+            if constexpr (KV8) {
+              tma_load_3d(&tm_q, &ring_full[stage], qdst, 0, 0, s.b * hkv + s.kvh, pol_keep);
+            } else {
+              // rows qi * group + g: query token qi, head kvh * group + g
+              tma_load_4d(&tm_q, &ring_full[stage], qdst, 0, s.kvh * group, 0, s.b, pol_keep);
+              tma_load_4d(&tm_q, &ring_full[stage], qdst + G::kQSlotBytes / 2, 64, s.kvh * group, 0,
+                          s.b, pol_keep);
+            }
           }
         }
         __syncwarp();
@@ -481,7 +510,8 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
           const CUtensorMap* m = tail ? map_tail : map_full;
           uint8_t* dst = sdst + operand_off + lane * box * 128;
           tma_load_4d(m, &ring_full[stage], dst, 0, s.kvh, off, page_id, pol_stream);
-          tma_load_4d(m, &ring_full[stage], dst + kHalfBytes, 64, s.kvh, off, page_id, pol_stream);
+          if constexpr (!KV8)
+            tma_load_4d(m, &ring_full[stage], dst + G::kHalfBytes, 64, s.kvh, off, page_id, pol_stream);
         }
         __syncwarp();
       }
@@ -521,28 +551,42 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     constexpr bool kBf16 = DType<T>::kBf16;
     constexpr uint32_t idesc_qk = make_idesc(kBf16, false, false, 128, kMaxGroup);
     constexpr uint32_t idesc_pv = make_idesc(kBf16, true, true, 128, kPvN);
+    constexpr uint32_t idesc_qk8 = make_idesc_e4m3(false, false, 128, 3 * kMaxGroup);
+    constexpr uint32_t idesc_pv8 = make_idesc_e4m3(true, true, 128, 3 * kMaxGroup);
     for (int64_t i = 0;; ++i) {
       int st = 1;
       if (lane == 0) {
-        const int stage = static_cast<int>(i % kStages);
-        const uint32_t ring_ph = static_cast<uint32_t>((i / kStages) & 1);
+        const int stage = static_cast<int>(i % G::kStages);
+        const uint32_t ring_ph = static_cast<uint32_t>((i / G::kStages) & 1);
         if (is_qk) {
-          const int sb = static_cast<int>(i % kSBufs);
+          const int sb = static_cast<int>(i % G::kSBufs);
           st = issue_wait(&kfull[stage], ring_ph, i);
-          if (st == 1) st = issue_wait(&s_empty[sb], static_cast<uint32_t>(((i / kSBufs) & 1) ^ 1), i);
+          if (st == 1) st = issue_wait(&s_empty[sb], static_cast<uint32_t>(((i / G::kSBufs) & 1) ^ 1), i);
           if (st == 1) {
             tc_fence_after();
-            const uint32_t kaddr = smem_u32(stages + stage * kStageBytes);
-            const uint32_t qaddr = kaddr + 2 * kOperandBytes;
+            const uint32_t kaddr = smem_u32(stages + stage * G::kStageBytes);
+            const uint32_t qaddr = kaddr + 2 * G::kOperandBytes;
+            if constexpr (KV8) {
 #pragma unroll
-            for (int j = 0; j < kHeadDim / 16; ++j) {
-              // A = K tile, K-major 128B swizzle: 8-row groups 1 KB apart; the
-              // 16-dim step j moves 32 B inside a 128 B row, 64-dim halves 16 KB apart.
-              const uint64_t a =
-                  make_sdesc(kaddr + (j >> 2) * kHalfBytes + (j & 3) * 32, 16, 1024, kLayoutSw128);
-              const uint64_t b = make_sdesc(qaddr + (j >> 2) * (kQSlotBytes / 2) + (j & 3) * 32, 16,
-                                            1024, kLayoutSw128);
-              umma_f16(tmem + col_s(sb), a, b, idesc_qk, j > 0 ? 1u : 0u);
+              for (int j = 0; j < kHeadDim / 32; ++j) {
+                // A = e4m3 K tile, K-major 128B swizzle: one 128 B row holds all
+                // 128 dims; the 32-dim step j moves 32 B inside the row.  B = the
+                // 48 rows of query parts, same layout.
+                const uint64_t a = make_sdesc(kaddr + j * 32, 16, 1024, kLayoutSw128);
+                const uint64_t b = make_sdesc(qaddr + j * 32, 16, 1024, kLayoutSw128);
+                umma_f8(tmem + G::col_s(sb), a, b, idesc_qk8, j > 0 ? 1u : 0u);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < kHeadDim / 16; ++j) {
+                // A = K tile, K-major 128B swizzle: 8-row groups 1 KB apart; the
+                // 16-dim step j moves 32 B inside a 128 B row, 64-dim halves 16 KB apart.
+                const uint64_t a =
+                    make_sdesc(kaddr + (j >> 2) * G::kHalfBytes + (j & 3) * 32, 16, 1024, kLayoutSw128);
+                const uint64_t b = make_sdesc(qaddr + (j >> 2) * (G::kQSlotBytes / 2) + (j & 3) * 32, 16,
+                                              1024, kLayoutSw128);
+                umma_f16(tmem + G::col_s(sb), a, b, idesc_qk, j > 0 ? 1u : 0u);
+              }
             }
             umma_commit(&s_full[sb]);
             umma_commit(&kempty[stage]);
@@ -553,17 +597,30 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
           if (st == 1) st = issue_wait(&vfull[stage], ring_ph, i);
           if (st == 1) {
             tc_fence_after();
-            const uint32_t vaddr = smem_u32(stages + stage * kStageBytes + kOperandBytes);
-            const uint32_t paddr = smem_u32(pbufs + pb * kPBufBytes);
+            const uint32_t vaddr = smem_u32(stages + stage * G::kStageBytes + G::kOperandBytes);
+            const uint32_t paddr = smem_u32(pbufs + pb * G::kPBufBytes);
+            if constexpr (KV8) {
 #pragma unroll
-            for (int j = 0; j < kTileTokens / 16; ++j) {
-              // A = V^T: MN-major (head-dim contiguous), 128B swizzle; the two
-              // 64-dim halves are 16 KB apart (LBO), 8-token groups 1 KB apart (SBO).
-              const uint64_t a = make_sdesc(vaddr + j * 2048, kHalfBytes, 1024, kLayoutSw128);
-              // B = [P_hi | P_lo]^T: MN-major (heads contiguous), no swizzle;
-              // 8-column core matrices 128 B apart (SBO), 8-token groups kPGroupBytes apart (LBO).
-              const uint64_t b = make_sdesc(paddr + j * 2 * kPGroupBytes, kPGroupBytes, 128, kLayoutNone);
-              umma_f16(tmem + col_o(pb), a, b, idesc_pv, j > 0 ? 1u : 0u);
+              for (int j = 0; j < kTileTokens / 32; ++j) {
+                // A = e4m3 V^T: MN-major, 128B swizzle, all 128 dims in one 128 B
+                // row (one swizzle atom along M), 8-token groups 1 KB apart (SBO).
+                const uint64_t a = make_sdesc(vaddr + j * 4096, G::kOperandBytes, 1024, kLayoutSw128);
+                // B = [P0 | P1 | P2]^T: MN-major, no swizzle; 16-column core
+                // matrices 128 B apart (SBO), 8-token groups 384 B apart (LBO).
+                const uint64_t b = make_sdesc(paddr + j * 4 * kPGroupBytes8, kPGroupBytes8, 128, kLayoutNone);
+                umma_f8(tmem + G::col_o(pb), a, b, idesc_pv8, j > 0 ? 1u : 0u);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < kTileTokens / 16; ++j) {
+                // A = V^T: MN-major (head-dim contiguous), 128B swizzle; the two
+                // 64-dim halves are 16 KB apart (LBO), 8-token groups 1 KB apart (SBO).
+                const uint64_t a = make_sdesc(vaddr + j * 2048, G::kHalfBytes, 1024, kLayoutSw128);
+                // B = [P_hi | P_lo]^T: MN-major (heads contiguous), no swizzle;
+                // 8-column core matrices 128 B apart (SBO), 8-token groups kPGroupBytes apart (LBO).
+                const uint64_t b = make_sdesc(paddr + j * 2 * kPGroupBytes, kPGroupBytes, 128, kLayoutNone);
+                umma_f16(tmem + G::col_o(pb), a, b, idesc_pv, j > 0 ? 1u : 0u);
+              }
             }
             umma_commit(&o_full[pb]);
             umma_commit(&vempty[stage]);
@@ -604,12 +661,26 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       const int pb = static_cast<int>(i & 1);
       mbar_wait_bounded(&o_full[pb], static_cast<uint32_t>((i >> 1) & 1), abort_flag, budget);
       tc_fence_after();
-      uint32_t r[kPvN];
-      if constexpr (NCOL == 8) tmem_ld_x16(lane_addr + col_o(pb), r); else tmem_ld_x32(lane_addr + col_o(pb), r);
-      tmem_wait_ld();
-      tc_fence_before();  // orders this load before the next P arrival (frees the O buffer)
+      if constexpr (KV8) {
+        // three parts of P, 16 columns apart: O = O0 + O1 / 16 + O2 / 256
+        uint32_t r0[NCOL], r1[NCOL], r2[NCOL];
+        tmem_ld_cols<NCOL>(lane_addr + G::col_o(pb), r0);
+        tmem_ld_cols<NCOL>(lane_addr + G::col_o(pb) + kMaxGroup, r1);
+        tmem_ld_cols<NCOL>(lane_addr + G::col_o(pb) + 2 * kMaxGroup, r2);
+        tmem_wait_ld();
+        tc_fence_before();  // orders this load before the next P arrival (frees the O buffer)
 #pragma unroll
-      for (int h = 0; h < NCOL; ++h) ov[h] = __uint_as_float(r[h]) + __uint_as_float(r[NCOL + h]);
+        for (int h = 0; h < NCOL; ++h)
+          ov[h] = fmaf(__uint_as_float(r2[h]), 1.f / 256.f,
+                       fmaf(__uint_as_float(r1[h]), 1.f / 16.f, __uint_as_float(r0[h])));
+      } else {
+        uint32_t r[kPvN];
+        if constexpr (NCOL == 8) tmem_ld_x16(lane_addr + G::col_o(pb), r); else tmem_ld_x32(lane_addr + G::col_o(pb), r);
+        tmem_wait_ld();
+        tc_fence_before();  // orders this load before the next P arrival (frees the O buffer)
+#pragma unroll
+        for (int h = 0; h < NCOL; ++h) ov[h] = __uint_as_float(r[h]) + __uint_as_float(r[NCOL + h]);
+      }
     };
     // Segment epilogue: direct output, or partial + (last arrival) merge.
     int fin_buf = 0;
@@ -655,11 +726,13 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
           p.lse[li] = v;
         }
       };
+      // e4m3 V: O carries 256 P (see the P split) times the stored V
+      const float osc = KV8 ? __ldg(p.v_scale + sg.kvh) * (1.f / 256.f) : 1.f;
       if (sg.nseg == 1) {
 #pragma unroll
         for (int h = 0; h < NCOL; ++h) {
           if (h < qrows) {
-            const float v = l_tot[h] > 0.f ? st.o[h] / l_tot[h] : 0.f;
+            const float v = l_tot[h] > 0.f ? st.o[h] * osc / l_tot[h] : 0.f;
             put_o(out_index(h), v);
             if (d == h)
               put_lse(lse_index(h),
@@ -673,7 +746,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
 #pragma unroll
       for (int h = 0; h < NCOL; ++h) {
         if (h < qrows) {
-          po[h * kHeadDim] = l_tot[h] > 0.f ? st.o[h] / l_tot[h] : 0.f;
+          po[h * kHeadDim] = l_tot[h] > 0.f ? st.o[h] * osc / l_tot[h] : 0.f;
           if (d == h) p.part_lse[slot * qrows + h] = l_tot[h] > 0.f ? st.m[h] + fast_log2(l_tot[h]) : neg_inf;
         }
       }
@@ -695,7 +768,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       // from shared memory and only the independent partial-O loads remain.
       const int nl = sg.nseg * qrows;
       float* sl = reinterpret_cast<float*>(scratch);
-      const bool staged = nl <= kPBufBytes / 4;
+      const bool staged = nl <= G::kPBufBytes / 4;
       if (staged) {
         for (int i = d; i < nl; i += 128) sl[i] = __ldcg(p.part_lse + sbase * qrows + i);
         named_bar_sync(1, 128);
@@ -725,6 +798,9 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
 #pragma unroll
     for (int h = 0; h < NCOL; ++h) coff[h] = (MULTI && p.causal) ? (h / group) - (sq - 1) : 0;
 
+    // e4m3 K: per query row of the segment, softmax scale (log2) x K scale x
+    // the inverse of the row's query-part scale
+    float qf[KV8 ? NCOL : 1];
     State cur, prev;
     reset(cur);
     reset(prev);
@@ -743,22 +819,44 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         reset(cur);
         prev_open = true;
       }
+      if constexpr (KV8) {
+        if (t == 0) {
+          const float ks = __ldg(p.k_scale + seg.kvh) * p.scale_log2;
+          const float* qi = p.q_inv + (static_cast<int64_t>(seg.b) * hkv + seg.kvh) * kMaxGroup;
+#pragma unroll
+          for (int h = 0; h < NCOL; ++h) qf[h] = ks * __ldg(qi + h);
+        }
+      }
       // ---- softmax of tile `it`
       const int sb = static_cast<int>(it & 1);  // P buffer and max-exchange slot
-      const int stage = static_cast<int>(it % kStages);
+      const int stage = static_cast<int>(it % G::kStages);
       {
-        const int sbuf = static_cast<int>(it % kSBufs);
-        mbar_wait_bounded(&s_full[sbuf], static_cast<uint32_t>((it / kSBufs) & 1), abort_flag, budget);
+        const int sbuf = static_cast<int>(it % G::kSBufs);
+        mbar_wait_bounded(&s_full[sbuf], static_cast<uint32_t>((it / G::kSBufs) & 1), abort_flag, budget);
       }
       tc_fence_after();
       uint32_t r[NCOL];
+      float s8[KV8 ? NCOL : 1];
       {
-        const uint32_t cs = col_s(static_cast<int>(it % kSBufs));
-        if constexpr (NCOL == 8) tmem_ld_x8(lane_addr + cs, r); else tmem_ld_x16(lane_addr + cs, r);
+        const uint32_t cs = G::col_s(static_cast<int>(it % G::kSBufs));
+        if constexpr (KV8) {
+          // three parts of the query, 16 columns apart: S = S0 + S1 / 16 + S2 / 256
+          uint32_t r1[NCOL], r2[NCOL];
+          tmem_ld_cols<NCOL>(lane_addr + cs, r);
+          tmem_ld_cols<NCOL>(lane_addr + cs + kMaxGroup, r1);
+          tmem_ld_cols<NCOL>(lane_addr + cs + 2 * kMaxGroup, r2);
+          tmem_wait_ld();
+#pragma unroll
+          for (int h = 0; h < NCOL; ++h)
+            s8[h] = fmaf(__uint_as_float(r2[h]), 1.f / 256.f,
+                         fmaf(__uint_as_float(r1[h]), 1.f / 16.f, __uint_as_float(r[h])));
+        } else {
+          if constexpr (NCOL == 8) tmem_ld_x8(lane_addr + cs, r); else tmem_ld_x16(lane_addr + cs, r);
+          tmem_wait_ld();
+        }
       }
-      tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(&s_empty[it % kSBufs]);
+      mbar_arrive(&s_empty[it % G::kSBufs]);
 
       const int tok0 = (seg.tile0 + t) * kTileTokens;
       const int valid_rows = seg.seqlen - tok0;  // may exceed 128; <=0 only for empty sequences
@@ -769,7 +867,10 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       for (int h = 0; h < NCOL; ++h) {
         // causal: query row h sees keys up to its own position L - sq + qi
         const bool vis = MULTI ? row < valid_rows + coff[h] : valid;
-        sv[h] = vis ? __uint_as_float(r[h]) * p.scale_log2 : neg_inf;
+        if constexpr (KV8)
+          sv[h] = vis ? s8[h] * qf[h] : neg_inf;
+        else
+          sv[h] = vis ? __uint_as_float(r[h]) * p.scale_log2 : neg_inf;
         const float wm = warp_max_f32(sv[h]);
         if (lane == 0) red_t[quad * kMaxGroup + h] = wm;
       }
@@ -787,21 +888,41 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         cur.m[h] = m_new;
       }
       if (valid_rows < kTileTokens && !valid &&
-          mbar_wait_bounded(&vfull[stage], static_cast<uint32_t>((it / kStages) & 1), abort_flag, budget)) {
+          mbar_wait_bounded(&vfull[stage], static_cast<uint32_t>((it / G::kStages) & 1), abort_flag, budget)) {
         // Rows past the sequence end: stale or never-written data must not
         // reach P.V (0 * NaN), so zero this token's V row in the stage, after
         // the tile's V copy (whose last box may cover the row) has landed.
-        uint4* vrow0 = reinterpret_cast<uint4*>(stages + stage * kStageBytes + kOperandBytes + row * 128);
-        uint4* vrow1 = reinterpret_cast<uint4*>(stages + stage * kStageBytes + kOperandBytes + kHalfBytes + row * 128);
+        uint4* vrow0 = reinterpret_cast<uint4*>(stages + stage * G::kStageBytes + G::kOperandBytes + row * 128);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          vrow0[i] = make_uint4(0, 0, 0, 0);
-          vrow1[i] = make_uint4(0, 0, 0, 0);
+        for (int i = 0; i < 8; ++i) vrow0[i] = make_uint4(0, 0, 0, 0);
+        if constexpr (!KV8) {
+          uint4* vrow1 = reinterpret_cast<uint4*>(stages + stage * G::kStageBytes + G::kOperandBytes + G::kHalfBytes + row * 128);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) vrow1[i] = make_uint4(0, 0, 0, 0);
         }
       }
-      {
+      if constexpr (KV8) {
+        // This token's row of [P0 | P1 | P2], the e4m3 parts of 256 P (scaled
+        // so small probabilities stay above the e4m3 subnormal range):
+        // 16-column chunks 128 B apart.
+        uint8_t* prow = pbufs + sb * G::kPBufBytes + (row >> 3) * kPGroupBytes8 + (row & 7) * 16;
+        uint32_t w[8][3];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (2 * i < NCOL) {
+            e4m3_split2(pv[2 * i] * 256.f, pv[2 * i + 1] * 256.f, w[i]);
+          } else {
+            w[i][0] = w[i][1] = w[i][2] = 0u;
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 3; ++k)
+          *reinterpret_cast<uint4*>(prow + k * 128) =
+              make_uint4(w[0][k] | (w[1][k] << 16), w[2][k] | (w[3][k] << 16),
+                         w[4][k] | (w[5][k] << 16), w[6][k] | (w[7][k] << 16));
+      } else {
         // This token's row of [P_hi | P_lo]: 8-column chunks 128 B apart.
-        uint8_t* prow = pbufs + sb * kPBufBytes + (row >> 3) * kPGroupBytes + (row & 7) * 16;
+        uint8_t* prow = pbufs + sb * G::kPBufBytes + (row >> 3) * kPGroupBytes + (row & 7) * 16;
 #pragma unroll
         for (int c = 0; c < NCOL / 8; ++c) {
           uint4 hi, lo;
@@ -824,7 +945,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
 #pragma unroll
           for (int h = 0; h < NCOL; ++h) prev.o[h] = fmaf(prev.o[h], prev.a[h], ov[h]);
           // P.V(it-1) is done, so its P buffer is free until tile it+1's softmax
-          finish(prev_seg, prev, pbufs + ((it + 1) & 1) * kPBufBytes);
+          finish(prev_seg, prev, pbufs + ((it + 1) & 1) * G::kPBufBytes);
         } else {
 #pragma unroll
           for (int h = 0; h < NCOL; ++h) cur.o[h] = fmaf(cur.o[h], cur.a[h], ov[h]);
@@ -869,13 +990,14 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, G::kTmemCols);
   }
 }
 
-template <typename T, typename OutT, int NCOL, bool MULTI, bool XCHG = false>
+template <typename T, typename OutT, int NCOL, bool MULTI, bool XCHG = false, bool KV8 = false>
 cudaError_t launch_typed(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream) {
-  auto kern = decode_sm100_kernel<T, OutT, NCOL, MULTI, XCHG>;
+  using G = Geo<KV8>;
+  auto kern = decode_sm100_kernel<T, OutT, NCOL, MULTI, XCHG, KV8>;
   // The attribute is per device; setting it again is harmless.
   static unsigned long long configured = 0;
   int dev = 0;
@@ -883,14 +1005,14 @@ cudaError_t launch_typed(const TensorMaps& m, const DecodeParams& p, int grid, c
   if (e != cudaSuccess) return e;
   const unsigned long long bit = 1ull << (dev & 63);
   if ((__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & bit) == 0) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmemBytes);
     if (e != cudaSuccess) return e;
     __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(kSm100Threads);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.dynamicSmemBytes = G::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -898,6 +1020,18 @@ cudaError_t launch_typed(const TensorMaps& m, const DecodeParams& p, int grid, c
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, m.q, m.k, m.v, m.k16, m.v16, p);
+}
+
+// e4m3 K/V; T is the query type (its rows arrive pre-split into e4m3 parts).
+template <typename T, typename OutT>
+cudaError_t launch_ncol_kv8(const TensorMaps& m, const DecodeParams& p, int grid,
+                            cudaStream_t stream) {
+  const bool multi = p.seqlen_q > 1 || p.causal;
+  if (p.qrows <= 8)
+    return multi ? launch_typed<T, OutT, 8, true, false, true>(m, p, grid, stream)
+                 : launch_typed<T, OutT, 8, false, false, true>(m, p, grid, stream);
+  return multi ? launch_typed<T, OutT, 16, true, false, true>(m, p, grid, stream)
+               : launch_typed<T, OutT, 16, false, false, true>(m, p, grid, stream);
 }
 
 template <typename T, typename OutT>

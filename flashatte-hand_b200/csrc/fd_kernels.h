@@ -47,6 +47,12 @@ struct DecodeParams {
   int len_add;                // keys appended this step: attended length = max(seqlens[b], 0) + len_add
   int cost_tile, cost_seg;    // split cost model: fixed cost per tile and per pair, in
                               // units where a full tile's K/V bytes cost 8
+  // e4m3 K/V only: dequantisation scales per KV head (K = k8 * k_scale[h],
+  // V = v8 * v_scale[h]) and, per (sequence, KV head, query row), the
+  // inverse of the power-of-two scale the query row was split with.
+  const float* k_scale;
+  const float* v_scale;
+  const float* q_inv;         // [batch * num_heads_k * 16]
 };
 
 struct SimtParams {
@@ -71,8 +77,12 @@ struct AppendParams {
   int64_t bt_stride, num_blocks;
   int batch, seqlen_new, num_heads_k, head_dim, page, elem_bytes;
   int* skipped;  // nullable: incremented per (b, t) row that had no page to go to
+  const float* k_scale;  // e4m3 cache only: per-KV-head quantisation scales
+  const float* v_scale;
 };
 cudaError_t launch_append_kv(const AppendParams& p, cudaStream_t stream);
+// 16-bit new rows (src_dtype 0 bf16, 1 fp16) into an e4m3 cache: x / scale[h], head_dim % 8 == 0.
+cudaError_t launch_append_kv_e4m3(const AppendParams& p, int src_dtype, cudaStream_t stream);
 
 // Workspace carve-up for the tensor-core kernel.
 struct WorkspaceLayout {
@@ -93,10 +103,27 @@ cudaError_t launch_sm100_bf16(const TensorMaps& m, const DecodeParams& p, int gr
 cudaError_t launch_sm100_bf16_f32(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
 cudaError_t launch_sm100_fp16(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
 cudaError_t launch_sm100_fp16_f32(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
+// e4m3 K/V cache, query of type bf16 / fp16 (tm.q then maps the pre-split
+// e4m3 query parts, see launch_split_query), output of the query type or fp32.
+cudaError_t launch_sm100_kv8_bf16(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
+cudaError_t launch_sm100_kv8_bf16_f32(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
+cudaError_t launch_sm100_kv8_fp16(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
+cudaError_t launch_sm100_kv8_fp16_f32(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
+
+// Split every query row of q [B, sq, Hq, 128] (16-bit, dtype 0 = bf16,
+// 1 = fp16) into three e4m3 parts for the e4m3-cache kernel: for each
+// (sequence, KV head) a 48 x 128-byte block (rows part * 16 + r, r = qi *
+// group + g; rows r >= qrows zero) in q8 [B * Hkv, 48, 128], and the inverse
+// of each row's power-of-two scale in q_inv [B * Hkv, 16].
+cudaError_t launch_split_query(const void* q, int dtype, int batch, int seqlen_q, int num_heads,
+                               int num_heads_k, uint8_t* q8, float* q_inv, cudaStream_t stream);
 
 // Launchers.  dtype: 0 bf16, 1 fp16; out_fp32 selects an fp32 output.
 cudaError_t launch_decode_sm100(const TensorMaps& m, const DecodeParams& p, int dtype,
                                 bool out_fp32, int grid, cudaStream_t stream);
+// e4m3 K/V cache; q_dtype (0 bf16, 1 fp16) is the query's and the 16-bit output's type.
+cudaError_t launch_decode_sm100_kv8(const TensorMaps& m, const DecodeParams& p, int q_dtype,
+                                    bool out_fp32, int grid, cudaStream_t stream);
 cudaError_t launch_decode_simt(const SimtParams& p, int dtype, bool out_fp32, cudaStream_t stream);
 cudaError_t launch_combine_lse(const float* part_o, int64_t o_stride, const float* part_lse,
                                int64_t l_stride, int64_t n_parts, int64_t rows, int64_t head_dim,

@@ -177,6 +177,16 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
+// Same for kind::f8f6f4 (both operands e4m3 here): K = 32 per instruction.
+__device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05 op issued so far by this thread
 // has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -259,6 +269,13 @@ __device__ __forceinline__ float warp_max_f32(float v) {
 // Named barrier over `nthreads` threads (multiple of 32), id 1..15.
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// N consecutive 32-bit TMEM columns (N = 8 or 16) of this warp's lanes.
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
+  static_assert(N == 8 || N == 16, "8 or 16 columns");
+  if constexpr (N == 8) tmem_ld_x8(taddr, r); else tmem_ld_x16(taddr, r);
 }
 
 }  // namespace fd

@@ -28,6 +28,10 @@ SIGNATURES: dict[str, tuple] = {
                                 + [_i32, _i32, _f32, _i64, _vp]),
     "fd_decode_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
     "fd_append_kv_paged": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp] + [_i64] * 7 + [_i32, _vp]),
+    "fd_decode_paged_fp8": (_i32, [_vp] * 7 + [_i64] + [_vp] * 4 + [_i64] * 8
+                            + [_i32, _i32, _f32, _i32, _i64, _vp, _sz, _vp]),
+    "fd_decode_workspace_size_fp8": (_sz, [_i64, _i64, _i64, _i64, _i64]),
+    "fd_append_kv_paged_fp8": (_i32, [_vp] * 8 + [_i64] * 7 + [_i32, _vp]),
     "fd_decode_paged_kvappend": (_i32, [_vp] * 9 + [_i64] * 9 + [_i32, _i32, _f32, _i32, _i64, _vp,
                                                                 _sz, _vp]),
     "fd_combine_lse": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _vp, _vp]),
@@ -47,7 +51,7 @@ SIGNATURES: dict[str, tuple] = {
     "fd_version": (_c.c_char_p, []),
 }
 
-FD_DTYPE_BF16, FD_DTYPE_FP16, FD_DTYPE_FP32 = 0, 1, 2
+FD_DTYPE_BF16, FD_DTYPE_FP16, FD_DTYPE_FP32, FD_DTYPE_E4M3 = 0, 1, 2, 3
 FD_OK = 0
 STATUS_NAMES = {0: "FD_OK", 1: "FD_ERR_INVALID_ARG", 2: "FD_ERR_UNSUPPORTED",
                 3: "FD_ERR_WORKSPACE", 4: "FD_ERR_CUDA", 5: "FD_ERR_DEVICE_TIMEOUT"}

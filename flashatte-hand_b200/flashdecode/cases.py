@@ -159,6 +159,23 @@ def materialize(case: DecodeCase, device, seed: int = 0) -> dict:
                 block_table=case.block_table.to(dev))
 
 
+def materialize_e4m3(case: DecodeCase, device, seed: int = 0) -> dict:
+    """materialize() with an e4m3 K/V cache: the N(0, 1) K and V are stored as
+    e4m3(x / scale[h]) with per-KV-head scales in [1/64, 1/32) (so the values
+    use most of the e4m3 range); q stays case.dtype.  Adds k_scale, v_scale."""
+    t = materialize(case, device, seed=seed)
+    dev = torch.device(device)
+    g = torch.Generator().manual_seed(seed + 2)
+    ks = (1.0 + torch.rand(case.Hkv, generator=g)) / 64.0
+    vs = (1.0 + torch.rand(case.Hkv, generator=g)) / 64.0
+    t["k_scale"], t["v_scale"] = ks.to(dev), vs.to(dev)
+    for name, sc in (("k_cache", t["k_scale"]), ("v_cache", t["v_scale"])):
+        x = t[name]
+        t[name] = (x.float() / sc[:, None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+        del x
+    return t
+
+
 def lpt_partition(seqlens, world: int) -> list[list[int]]:
     """Longest-processing-time-first assignment of sequences to `world` shards."""
     order = sorted(range(len(seqlens)), key=lambda b: (-int(seqlens[b]), b))

@@ -70,7 +70,8 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                  max_seqlen_k: int | None = None, workspace: torch.Tensor | None = None,
                  stream: torch.cuda.Stream | None = None, lse: torch.Tensor | None = None,
                  causal: bool = False, k: torch.Tensor | None = None,
-                 v: torch.Tensor | None = None):
+                 v: torch.Tensor | None = None, k_scale: torch.Tensor | None = None,
+                 v_scale: torch.Tensor | None = None):
     """Paged decode attention for seqlen_q >= 1 query tokens per sequence.
 
     q [B, sq, Hq, D]; k_cache/v_cache [num_blocks, page, Hkv, D];
@@ -86,13 +87,24 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     positions cache_seqlens[b] .. cache_seqlens[b] + seqlen_new - 1, then
     attention runs over L = cache_seqlens[b] + seqlen_new keys;
     cache_seqlens itself is left unchanged.
+
+    FP8 cache: k_cache / v_cache of dtype torch.float8_e4m3fn with k_scale /
+    v_scale fp32 [Hkv] (the attended key is k_cache * k_scale[h]); q stays
+    bf16 or fp16 and k / v, when given, are 16-bit rows quantised into the
+    cache.  Head dim 128, seqlen_q * (Hq / Hkv) <= 16, pages of a multiple
+    of 16 tokens.
     """
     lib = load_library()
     _require_cuda(q, k_cache, v_cache, cache_seqlens, block_table)
     if q.dim() != 4:
         raise ValueError(f"q must be [B, seqlen_q, Hq, D], got {tuple(q.shape)}")
-    if q.dtype not in _DTYPES or k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
-        raise ValueError("q, k_cache, v_cache must share dtype bf16 or fp16")
+    kv8 = k_cache.dtype == torch.float8_e4m3fn
+    if q.dtype not in _DTYPES or v_cache.dtype != k_cache.dtype or (not kv8 and k_cache.dtype != q.dtype):
+        raise ValueError("q, k_cache, v_cache must share dtype bf16 or fp16 (or e4m3 caches)")
+    if kv8:
+        _check_scales(k_scale, v_scale, k_cache.shape[2])
+    elif k_scale is not None or v_scale is not None:
+        raise ValueError("k_scale / v_scale apply to float8_e4m3fn caches only")
     if cache_seqlens.dtype != torch.int32 or block_table.dtype != torch.int32:
         raise ValueError("cache_seqlens and block_table must be int32")
     for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache),
@@ -124,6 +136,18 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     st = stream if stream is not None else torch.cuda.current_stream(q.device)
     if (k is None) != (v is None):
         raise ValueError("k and v must be given together")
+    if kv8:
+        if k is not None:
+            _check_new_kv(k, v, k_cache, B, q.dtype)
+        with torch.cuda.device(q.device):
+            status = lib.fd_decode_paged_fp8(
+                _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(k_scale), _ptr(v_scale), _ptr(k),
+                _ptr(v), 0 if k is None else k.shape[1], _ptr(out), _ptr(lse), _ptr(cache_seqlens),
+                _ptr(block_table), int(block_table.shape[1]), B, sq, Hq, Hkv, D, page, num_blocks,
+                _DTYPES[q.dtype], _OUT_DTYPES[odt], scale, 1 if causal else 0,
+                int(max_seqlen_k or 0), ws_ptr, ws_bytes, st.cuda_stream)
+        check(status)
+        return (out, lse) if return_softmax_lse else out
     if k is not None:
         _check_new_kv(k, v, k_cache, B)
         with torch.cuda.device(q.device):
@@ -145,35 +169,63 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     return (out, lse) if return_softmax_lse else out
 
 
-def _check_new_kv(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, B: int) -> None:
+def _check_scales(k_scale, v_scale, Hkv: int) -> None:
+    for name, sc in (("k_scale", k_scale), ("v_scale", v_scale)):
+        if sc is None:
+            raise ValueError(f"{name} [Hkv] fp32 is required with a float8_e4m3fn cache")
+        _require_cuda(sc)
+        if sc.dtype != torch.float32 or sc.shape != (Hkv,) or not sc.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous fp32 [{Hkv}] tensor")
+
+
+def _check_new_kv(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, B: int,
+                  new_dtype: torch.dtype | None = None) -> None:
     _require_cuda(k, v)
     if k.dim() != 4 or tuple(v.shape) != tuple(k.shape):
         raise ValueError("k and v must both be [B, seqlen_new, Hkv, D]")
     if k.shape[0] != B or k.shape[2] != k_cache.shape[2] or k.shape[3] != k_cache.shape[3]:
         raise ValueError("k / v shape does not match the batch and cache heads")
-    if k.dtype != k_cache.dtype or v.dtype != k_cache.dtype:
-        raise ValueError("k / v must have the cache dtype")
+    want = k_cache.dtype if new_dtype is None else new_dtype
+    if k.dtype != want or v.dtype != want:
+        raise ValueError(f"k / v must be {want}")
     if not (k.is_contiguous() and v.is_contiguous()):
         raise ValueError("k and v must be contiguous")
 
 
 def append_kv(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
               cache_seqlens: torch.Tensor, block_table: torch.Tensor,
-              stream: torch.cuda.Stream | None = None) -> None:
+              stream: torch.cuda.Stream | None = None, k_scale: torch.Tensor | None = None,
+              v_scale: torch.Tensor | None = None) -> None:
     """Write k / v [B, seqlen_new, Hkv, D] into the paged cache at positions
-    cache_seqlens[b] + t (the cache update of flash_attn_with_kvcache)."""
+    cache_seqlens[b] + t (the cache update of flash_attn_with_kvcache).  For
+    float8_e4m3fn caches k / v are 16-bit and stored as e4m3(x / scale[h])
+    with the fp32 [Hkv] k_scale / v_scale."""
     lib = load_library()
     _require_cuda(k_cache, v_cache, cache_seqlens, block_table)
     if cache_seqlens.dtype != torch.int32 or block_table.dtype != torch.int32:
         raise ValueError("cache_seqlens and block_table must be int32")
     if not (k_cache.is_contiguous() and v_cache.is_contiguous() and block_table.is_contiguous()):
         raise ValueError("caches and block_table must be contiguous")
-    if k_cache.dtype not in _DTYPES or tuple(v_cache.shape) != tuple(k_cache.shape):
-        raise ValueError("k_cache/v_cache must be bf16 or fp16 with equal shapes")
+    kv8 = k_cache.dtype == torch.float8_e4m3fn
+    if (k_cache.dtype not in _DTYPES and not kv8) or v_cache.dtype != k_cache.dtype \
+            or tuple(v_cache.shape) != tuple(k_cache.shape):
+        raise ValueError("k_cache/v_cache must be bf16, fp16 or float8_e4m3fn with equal shapes")
     B = block_table.shape[0]
-    _check_new_kv(k, v, k_cache, B)
     num_blocks, page, Hkv, D = k_cache.shape
     st = stream if stream is not None else torch.cuda.current_stream(k.device)
+    if kv8:
+        _check_scales(k_scale, v_scale, Hkv)
+        if k.dtype not in _DTYPES:
+            raise ValueError("k / v must be bf16 or fp16")
+        _check_new_kv(k, v, k_cache, B, k.dtype)
+        with torch.cuda.device(k.device):
+            status = lib.fd_append_kv_paged_fp8(
+                _ptr(k), _ptr(v), _ptr(k_cache), _ptr(v_cache), _ptr(k_scale), _ptr(v_scale),
+                _ptr(cache_seqlens), _ptr(block_table), int(block_table.shape[1]), B, k.shape[1],
+                Hkv, D, page, num_blocks, _DTYPES[k.dtype], st.cuda_stream)
+        check(status)
+        return
+    _check_new_kv(k, v, k_cache, B)
     with torch.cuda.device(k.device):
         status = lib.fd_append_kv_paged(
             _ptr(k), _ptr(v), _ptr(k_cache), _ptr(v_cache), _ptr(cache_seqlens), _ptr(block_table),

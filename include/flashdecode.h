@@ -28,6 +28,7 @@ extern "C" {
 #define FD_DTYPE_BF16 0
 #define FD_DTYPE_FP16 1
 #define FD_DTYPE_FP32 2 /* output only */
+#define FD_DTYPE_E4M3 3 /* K/V cache only (fd_decode_paged_fp8) */
 
 /* status codes */
 #define FD_OK 0
@@ -154,6 +155,51 @@ int fd_decode_paged_kvappend(const void* q, void* k_cache, void* v_cache, const 
                              int dtype, int out_dtype, float softmax_scale, int causal,
                              int64_t max_seqlen_k, void* workspace, size_t workspace_bytes,
                              void* stream);
+
+/*
+ * fd_decode_paged_fp8 - decode over an e4m3 (FP8) KV cache with per-KV-head
+ * scales: the attended key/value of token t, KV head h, is
+ * k_cache[...] * k_scale[h] / v_cache[...] * v_scale[h].
+ *
+ * Replaces: nothing in the reference (its caches are bf16, best :1186-1211);
+ * this is the FP8-cache extension of the same decode, halving the bytes the
+ * HBM-bound kernel reads.  q (bf16 or fp16, q_dtype), out (q_dtype or fp32)
+ * and lse keep fd_decode_paged_mq's layouts and meaning; k_cache / v_cache
+ * are [num_blocks, page, Hkv, 128] e4m3 bytes; k_scale / v_scale are device
+ * fp32 [Hkv].  With k_new / v_new (16-bit [B, seqlen_new, Hkv, 128]) given,
+ * they are first quantised into the cache at cache_seqlens[b] + t as by
+ * fd_append_kv_paged_fp8 and attention covers cache_seqlens[b] + seqlen_new
+ * keys; pass NULL for both otherwise.  Supported: head dim 128,
+ * seqlen_q * (Hq / Hkv) <= 16, page a multiple of 16, 16-byte aligned
+ * q / caches (FD_ERR_UNSUPPORTED otherwise).  Workspace: at least
+ * fd_decode_workspace_size_fp8(...) bytes, 256-byte aligned, or NULL.
+ */
+int fd_decode_paged_fp8(const void* q, void* k_cache, void* v_cache, const float* k_scale,
+                        const float* v_scale, const void* k_new, const void* v_new,
+                        int64_t seqlen_new, void* out, float* lse, const int32_t* cache_seqlens,
+                        const int32_t* block_table, int64_t block_table_stride,
+                        int64_t batch_size, int64_t seqlen_q, int64_t num_heads,
+                        int64_t num_heads_k, int64_t headdim, int64_t page_block_size,
+                        int64_t num_blocks, int q_dtype, int out_dtype, float softmax_scale,
+                        int causal, int64_t max_seqlen_k, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+/* Workspace bytes fd_decode_paged_fp8 needs (0 for unsupported shapes). */
+size_t fd_decode_workspace_size_fp8(int64_t batch_size, int64_t seqlen_q, int64_t num_heads,
+                                    int64_t num_heads_k, int64_t headdim);
+
+/*
+ * fd_append_kv_paged_fp8 - fd_append_kv_paged into an e4m3 cache: each new
+ * 16-bit value x (src_dtype bf16 or fp16) of KV head h is stored as
+ * e4m3(x / scale[h]), rounded to nearest even and saturated at +-448.
+ * Replaces: nothing in the reference (see fd_decode_paged_fp8).
+ */
+int fd_append_kv_paged_fp8(const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                           const float* k_scale, const float* v_scale,
+                           const int32_t* cache_seqlens, const int32_t* block_table,
+                           int64_t block_table_stride, int64_t batch_size, int64_t seqlen_new,
+                           int64_t num_heads_k, int64_t headdim, int64_t page_block_size,
+                           int64_t num_blocks, int src_dtype, void* stream);
 
 /*
  * fd_decode_paged_noalloc - fd_decode_paged for callers that cannot allocate

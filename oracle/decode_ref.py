@@ -142,6 +142,30 @@ def append_reference(k_cache: torch.Tensor, v_cache: torch.Tensor, k_new: torch.
     return kc, vc, (lens + sn).to(torch.int32)
 
 
+def quantize_e4m3(x: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """e4m3 (float8_e4m3fn) of x / scale[h] for x [..., Hkv, D], scale [Hkv]:
+    fp32 division, round to nearest even, saturated at +-448 (the FP8 cache
+    format of the operator's fd_append_kv_paged_fp8; the reference has no FP8
+    path)."""
+    q = x.cpu().float() / scale.cpu().float()[:, None]
+    return q.clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+
+
+def dequantize_e4m3(c: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """fp32 values of an e4m3 cache [..., Hkv, D] with per-KV-head scales."""
+    return c.cpu().float() * scale.cpu().float()[:, None]
+
+
+def append_reference_e4m3(k_cache, v_cache, k_new, v_new, k_scale, v_scale, cache_seqlens,
+                          block_table):
+    """append_reference for an e4m3 cache: new rows are quantised first."""
+    kq = quantize_e4m3(k_new, k_scale).view(torch.uint8)
+    vq = quantize_e4m3(v_new, v_scale).view(torch.uint8)
+    kc, vc, lens = append_reference(k_cache.cpu().view(torch.uint8), v_cache.cpu().view(torch.uint8),
+                                    kq, vq, cache_seqlens, block_table)
+    return kc.view(torch.float8_e4m3fn), vc.view(torch.float8_e4m3fn), lens
+
+
 def merge_partials(part_o: torch.Tensor, part_lse: torch.Tensor):
     """Merge normalised partials over disjoint KV ranges (natural-log LSE).
 
