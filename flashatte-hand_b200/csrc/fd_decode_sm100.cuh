@@ -306,8 +306,12 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
                         const __grid_constant__ CUtensorMap tm_k16,
                         const __grid_constant__ CUtensorMap tm_v16, const DecodeParams p) {
   using G = Geo<KV8>;
-  // P.V uses N = 2*NCOL columns: NCOL hi parts then NCOL lo parts of P.
-  constexpr int kPvN = 2 * NCOL;
+  // 16-bit P.V uses N = 2*NL columns: NL hi parts then NL lo parts of P.
+  // NCOL query rows are computed per (sequence, KV head); the 16-bit P
+  // layout holds NL >= 8 columns per part (a UMMA needs N >= 16), the
+  // columns past NCOL being zero.
+  constexpr int NL = NCOL < 8 ? 8 : NCOL;
+  constexpr int kPvN = 2 * NL;
   constexpr int kPGroupBytes = (kPvN / 8) * 128;  // one 8-token group of P rows
   constexpr int kPGroupBytes8 = 3 * 128;           // the same for the three e4m3 parts of P
   extern __shared__ uint8_t smem_raw[];
@@ -675,11 +679,11 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
                        fmaf(__uint_as_float(r1[h]), 1.f / 16.f, __uint_as_float(r0[h])));
       } else {
         uint32_t r[kPvN];
-        if constexpr (NCOL == 8) tmem_ld_x16(lane_addr + G::col_o(pb), r); else tmem_ld_x32(lane_addr + G::col_o(pb), r);
+        if constexpr (NL == 8) tmem_ld_x16(lane_addr + G::col_o(pb), r); else tmem_ld_x32(lane_addr + G::col_o(pb), r);
         tmem_wait_ld();
         tc_fence_before();  // orders this load before the next P arrival (frees the O buffer)
 #pragma unroll
-        for (int h = 0; h < NCOL; ++h) ov[h] = __uint_as_float(r[h]) + __uint_as_float(r[NCOL + h]);
+        for (int h = 0; h < NCOL; ++h) ov[h] = __uint_as_float(r[h]) + __uint_as_float(r[NL + h]);
       }
     };
     // Segment epilogue: direct output, or partial + (last arrival) merge.
@@ -851,7 +855,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
             s8[h] = fmaf(__uint_as_float(r2[h]), 1.f / 256.f,
                          fmaf(__uint_as_float(r1[h]), 1.f / 16.f, __uint_as_float(r[h])));
         } else {
-          if constexpr (NCOL == 8) tmem_ld_x8(lane_addr + cs, r); else tmem_ld_x16(lane_addr + cs, r);
+          tmem_ld_cols<NCOL>(lane_addr + cs, r);
           tmem_wait_ld();
         }
       }
@@ -924,14 +928,18 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         // This token's row of [P_hi | P_lo]: 8-column chunks 128 B apart.
         uint8_t* prow = pbufs + sb * G::kPBufBytes + (row >> 3) * kPGroupBytes + (row & 7) * 16;
 #pragma unroll
-        for (int c = 0; c < NCOL / 8; ++c) {
-          uint4 hi, lo;
-          DType<T>::split2(pv[8 * c + 0], pv[8 * c + 1], hi.x, lo.x);
-          DType<T>::split2(pv[8 * c + 2], pv[8 * c + 3], hi.y, lo.y);
-          DType<T>::split2(pv[8 * c + 4], pv[8 * c + 5], hi.z, lo.z);
-          DType<T>::split2(pv[8 * c + 6], pv[8 * c + 7], hi.w, lo.w);
-          *reinterpret_cast<uint4*>(prow + c * 128) = hi;
-          *reinterpret_cast<uint4*>(prow + (NCOL / 8 + c) * 128) = lo;
+        for (int c = 0; c < NL / 8; ++c) {
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (8 * c + 2 * j < NCOL) {
+              DType<T>::split2(pv[8 * c + 2 * j], pv[8 * c + 2 * j + 1], hw[j], lw[j]);
+            } else {
+              hw[j] = lw[j] = 0u;
+            }
+          }
+          *reinterpret_cast<uint4*>(prow + c * 128) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4*>(prow + (NL / 8 + c) * 128) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
         }
       }
       fence_proxy_async_smem();
@@ -1027,6 +1035,9 @@ template <typename T, typename OutT>
 cudaError_t launch_ncol_kv8(const TensorMaps& m, const DecodeParams& p, int grid,
                             cudaStream_t stream) {
   const bool multi = p.seqlen_q > 1 || p.causal;
+  if (p.qrows <= 4)
+    return multi ? launch_typed<T, OutT, 4, true, false, true>(m, p, grid, stream)
+                 : launch_typed<T, OutT, 4, false, false, true>(m, p, grid, stream);
   if (p.qrows <= 8)
     return multi ? launch_typed<T, OutT, 8, true, false, true>(m, p, grid, stream)
                  : launch_typed<T, OutT, 8, false, false, true>(m, p, grid, stream);
@@ -1046,6 +1057,9 @@ cudaError_t launch_ncol(const TensorMaps& m, const DecodeParams& p, int grid, cu
                    : launch_typed<T, float, 16, false, true>(m, p, grid, stream);
     }
   }
+  if (p.qrows <= 4)
+    return multi ? launch_typed<T, OutT, 4, true>(m, p, grid, stream)
+                 : launch_typed<T, OutT, 4, false>(m, p, grid, stream);
   if (p.qrows <= 8)
     return multi ? launch_typed<T, OutT, 8, true>(m, p, grid, stream)
                  : launch_typed<T, OutT, 8, false>(m, p, grid, stream);

@@ -196,6 +196,13 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld_x4(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr)
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t (&r)[8]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
@@ -271,11 +278,13 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// N consecutive 32-bit TMEM columns (N = 8 or 16) of this warp's lanes.
+// N consecutive 32-bit TMEM columns (N = 4, 8 or 16) of this warp's lanes.
 template <int N>
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
-  static_assert(N == 8 || N == 16, "8 or 16 columns");
-  if constexpr (N == 8) tmem_ld_x8(taddr, r); else tmem_ld_x16(taddr, r);
+  static_assert(N == 4 || N == 8 || N == 16, "4, 8 or 16 columns");
+  if constexpr (N == 4) tmem_ld_x4(taddr, r);
+  else if constexpr (N == 8) tmem_ld_x8(taddr, r);
+  else tmem_ld_x16(taddr, r);
 }
 
 }  // namespace fd
