@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="budget of the cpu_baseline leg (rank 0, N=1)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--kv", default="native", choices=["native", "fp8"],
+                    help="K/V cache storage: the config's dtype, or e4m3 with per-head scales")
     return ap.parse_args()
 
 
@@ -235,6 +237,15 @@ def main():
         total_kv = full.kv_bytes()
         t = cases.materialize(case, "cuda", seed=0)  # same q on every rank
         splitter = fdist.PeerSplitKVDecode(case.B, case.Hq, case.D, case.dtype, "cuda")
+    fp8 = args.kv == "fp8"
+    if fp8:
+        if splitter is not None:
+            raise SystemExit("--kv fp8 runs the single-GPU and batch-sharded modes only")
+        del t
+        torch.cuda.empty_cache()
+        t = cases.materialize_e4m3(case, "cuda", seed=rank)
+        total_kv //= 2
+    kv_kw = dict(k_scale=t["k_scale"], v_scale=t["v_scale"]) if fp8 else {}
     max_len = max(int(case.seqlens.max()), 1)
 
     def decode(q, seqlens, bt):
@@ -242,7 +253,7 @@ def main():
             return splitter(q, t["k_cache"], t["v_cache"], seqlens, bt, case.softmax_scale)
         return flashdecode.flash_decode(q, t["k_cache"], t["v_cache"], seqlens, bt,
                                         softmax_scale=case.softmax_scale, return_softmax_lse=True,
-                                        max_seqlen_k=max_len)
+                                        max_seqlen_k=max_len, **kv_kw)
 
     def step():
         decode(t["q"], t["cache_seqlens"], t["block_table"])
@@ -349,16 +360,16 @@ def main():
 
     per_call_s = ms * 1e-3 / args.steps
     kv_gbs = total_kv / per_call_s / 1e9
-    alg_per_launch = case.algorithmic_bytes(with_lse=True)
+    alg_per_launch = case.algorithmic_bytes(with_lse=True) - (case.kv_bytes() // 2 if fp8 else 0)
     achieved = alg_per_launch / per_call_s / 1e9
     peak, peak_kind = peaks()
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4),
-                "traffic": profile_traffic(f"cfg{args.config}") if world == 1 else None,
+                "traffic": profile_traffic(f"cfg{args.config}") if world == 1 and not fp8 else None,
                 "peak_source": peak_kind, "kernel": "decode_sm100_kernel",
                 "alg_bytes_per_launch": alg_per_launch}
     cpu = None
-    if world == 1 and args.cpu_seconds > 0:
+    if world == 1 and args.cpu_seconds > 0 and not fp8:
         ct = {k: v.cpu() for k, v in t.items()}
         rate, nseq, dt = cpu_oracle_rate(case, ct, args.cpu_seconds)
         cpu = {"value": round(rate, 4), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
@@ -369,13 +380,15 @@ def main():
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_call_s * 1e3, 5),
         "us_per_call": round(per_call_s * 1e6, 2), "pct_of_peak": round(100 * kv_gbs / world / peak, 2),
         "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
-        "dtype": "bf16" if case.dtype == torch.bfloat16 else "fp16", "data": "synthetic",
-        "config": {"workload": full.name, "global_batch": full.B * (world if scaling == "weak" else 1),
+        "dtype": ("e4m3-kv/" if fp8 else "") + ("bf16" if case.dtype == torch.bfloat16 else "fp16"),
+        "data": "synthetic",
+        "config": {"workload": full.name + ("_e4m3kv" if fp8 else ""),
+                   "global_batch": full.B * (world if scaling == "weak" else 1),
                    "seq_len": int(full.seqlens.max()), "parallelism": parallel,
                    "Hq": full.Hq, "Hkv": full.Hkv, "head_dim": full.D, "page": full.page,
                    "l2": "inputs larger than L2 (KV cache > 126 MB), no flush"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-        "gpu_launches": launches_per_call * args.steps, "clocks": clk.summary(),
+        "gpu_launches": (launches_per_call + (1 if fp8 else 0)) * args.steps, "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
 

@@ -777,22 +777,50 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         for (int i = d; i < nl; i += 128) sl[i] = __ldcg(p.part_lse + sbase * qrows + i);
         named_bar_sync(1, 128);
       }
-      for (int h = 0; h < qrows; ++h) {
-        auto lse_of = [&](int j) {
-          return staged ? sl[j * qrows + h] : __ldcg(p.part_lse + (sbase + j) * qrows + h);
-        };
-        float mx = neg_inf;
-        for (int j = 0; j < sg.nseg; ++j) mx = fmaxf(mx, lse_of(j));
-        float den = 0.f, acc = 0.f;
+      // Segment-outer, row-inner: each step loads one partial value of every
+      // query row (independent loads, several steps in flight), so a pair cut
+      // into many segments merges in a few L2 round trips rather than one per
+      // (segment, row).
+      auto lse_of = [&](int j, int h) {
+        return staged ? sl[j * qrows + h] : __ldcg(p.part_lse + (sbase + j) * qrows + h);
+      };
+      float mx[NCOL], den[NCOL], acc[NCOL];
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) {
+        mx[h] = neg_inf;
+        den[h] = 0.f;
+        acc[h] = 0.f;
+      }
+      for (int j = 0; j < sg.nseg; ++j) {
+#pragma unroll
+        for (int h = 0; h < NCOL; ++h)
+          if (h < qrows) mx[h] = fmaxf(mx[h], lse_of(j, h));
+      }
+      const float* po_d = p.part_o + sbase * qrows * kHeadDim + d;
 #pragma unroll 4
-        for (int j = 0; j < sg.nseg; ++j) {
-          const float lj = lse_of(j);
-          const float wj = lj == neg_inf ? 0.f : fast_exp2(lj - mx);  // empty parts hold O = 0
-          acc = fmaf(wj, __ldcg(p.part_o + ((sbase + j) * qrows + h) * kHeadDim + d), acc);
-          den += wj;
+      for (int j = 0; j < sg.nseg; ++j) {
+        float o[NCOL];
+#pragma unroll
+        for (int h = 0; h < NCOL; ++h)
+          o[h] = h < qrows ? __ldcg(po_d + (static_cast<int64_t>(j) * qrows + h) * kHeadDim) : 0.f;
+#pragma unroll
+        for (int h = 0; h < NCOL; ++h) {
+          if (h < qrows) {
+            const float lj = lse_of(j, h);
+            const float wj = lj == neg_inf ? 0.f : fast_exp2(lj - mx[h]);  // empty parts hold O = 0
+            acc[h] = fmaf(wj, o[h], acc[h]);
+            den[h] += wj;
+          }
         }
-        put_o(out_index(h), den > 0.f ? acc / den : 0.f);
-        if (d == 0) put_lse(lse_index(h), den > 0.f ? (mx + fast_log2(den)) * 0.69314718055994531f : neg_inf);
+      }
+#pragma unroll
+      for (int h = 0; h < NCOL; ++h) {
+        if (h < qrows) {
+          put_o(out_index(h), den[h] > 0.f ? acc[h] / den[h] : 0.f);
+          if (d == 0)
+            put_lse(lse_index(h),
+                    den[h] > 0.f ? (mx[h] + fast_log2(den[h])) * 0.69314718055994531f : neg_inf);
+        }
       }
     };
 
