@@ -365,7 +365,8 @@ def main():
     peak, peak_kind = peaks()
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4),
-                "traffic": profile_traffic(f"cfg{args.config}") if world == 1 and not fp8 else None,
+                "traffic": (profile_traffic(f"cfg{args.config}" + ("_e4m3kv" if fp8 else ""))
+                            if world == 1 else None),
                 "peak_source": peak_kind, "kernel": "decode_sm100_kernel",
                 "alg_bytes_per_launch": alg_per_launch}
     cpu = None
