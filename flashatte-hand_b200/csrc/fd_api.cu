@@ -143,6 +143,54 @@ CUresult encode(CUtensorMap* m, int dtype, int rank, const void* base, const cuu
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
+// K and V tensor maps ([num_blocks, page, Hkv, 128] caches; boxes of `chunk`
+// tokens for full tiles and 16 for partial ones).  Encoding a map is pure host
+// work that costs about as much as a small decode call, and a decode loop
+// passes the same caches every step, so each thread keeps the maps of its
+// last call and re-encodes only when pointers or shape change.
+struct KvMapKey {
+  const void* k;
+  const void* v;
+  int64_t hkv, page, nblk;
+  int dtype, chunk;
+  bool operator==(const KvMapKey& o) const {
+    return k == o.k && v == o.v && hkv == o.hkv && page == o.page && nblk == o.nblk &&
+           dtype == o.dtype && chunk == o.chunk;
+  }
+};
+
+CUresult kv_maps(fd::TensorMaps& m, int dtype, const void* k, const void* v, int64_t hkv,
+                 int64_t page, int64_t nblk, int chunk) {
+  thread_local KvMapKey key{};
+  thread_local CUtensorMap cached[4];
+  thread_local bool valid = false;
+  const KvMapKey want{k, v, hkv, page, nblk, dtype, chunk};
+  if (!(valid && key == want)) {
+    const bool e4m3 = dtype == FD_DTYPE_E4M3;
+    const cuuint64_t es = e4m3 ? 1 : 2;
+    const cuuint64_t dims[4] = {128, (cuuint64_t)hkv, (cuuint64_t)page, (cuuint64_t)nblk};
+    const cuuint64_t strides[3] = {128 * es, (cuuint64_t)hkv * 128 * es,
+                                   (cuuint64_t)(page * hkv) * 128 * es};
+    // 16-bit rows are loaded as two 64-dim halves, e4m3 rows whole
+    const cuuint32_t bx = e4m3 ? 128 : 64;
+    const cuuint32_t box[4] = {bx, 1, (cuuint32_t)chunk, 1};
+    const cuuint32_t box16[4] = {bx, 1, 16, 1};
+    valid = false;
+    CUresult r = encode(&cached[0], dtype, 4, k, dims, strides, box);
+    if (r == CUDA_SUCCESS) r = encode(&cached[1], dtype, 4, v, dims, strides, box);
+    if (r == CUDA_SUCCESS) r = encode(&cached[2], dtype, 4, k, dims, strides, box16);
+    if (r == CUDA_SUCCESS) r = encode(&cached[3], dtype, 4, v, dims, strides, box16);
+    if (r != CUDA_SUCCESS) return r;
+    key = want;
+    valid = true;
+  }
+  m.k = cached[0];
+  m.v = cached[1];
+  m.k16 = cached[2];
+  m.v16 = cached[3];
+  return CUDA_SUCCESS;
+}
+
 // Launch epoch for the split-pair arrival counters: consecutive launches get
 // different values in 1 .. 2^20-1 (0 never occurs, so a zeroed workspace
 // reads as "no arrivals").
@@ -346,16 +394,8 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
 
   fd::TensorMaps maps;
   {
-    const cuuint64_t dims[4] = {128, (cuuint64_t)num_heads_k, (cuuint64_t)page_block_size,
-                                (cuuint64_t)num_blocks};
-    const cuuint64_t strides[3] = {(cuuint64_t)(128 * es), (cuuint64_t)(num_heads_k * 128 * es),
-                                   (cuuint64_t)(page_block_size * num_heads_k * 128 * es)};
-    const cuuint32_t box[4] = {64, 1, (cuuint32_t)chunk, 1};
-    const cuuint32_t box16[4] = {64, 1, 16, 1};
-    CUresult r = encode(&maps.k, dtype, 4, k_cache, dims, strides, box);
-    if (r == CUDA_SUCCESS) r = encode(&maps.v, dtype, 4, v_cache, dims, strides, box);
-    if (r == CUDA_SUCCESS) r = encode(&maps.k16, dtype, 4, k_cache, dims, strides, box16);
-    if (r == CUDA_SUCCESS) r = encode(&maps.v16, dtype, 4, v_cache, dims, strides, box16);
+    const CUresult r = kv_maps(maps, dtype, k_cache, v_cache, num_heads_k, page_block_size,
+                               num_blocks, chunk);
     if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "K/V tensor map encode failed (%d)", (int)r);
   }
 
@@ -376,7 +416,22 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
       const cuuint64_t strides[3] = {(cuuint64_t)(128 * es), (cuuint64_t)(num_heads * 128 * es),
                                      (cuuint64_t)(seqlen_q * num_heads * 128 * es)};
       const cuuint32_t box[4] = {64, (cuuint32_t)group, (cuuint32_t)seqlen_q, 1};
-      const CUresult r = encode(&maps.q, dtype, 4, qb, dims, strides, box);
+      // same per-thread reuse as the K/V maps: the query buffer is usually
+      // the same from step to step
+      thread_local const void* q_key_ptr = nullptr;
+      thread_local int64_t q_key[5] = {0, 0, 0, 0, 0};
+      thread_local CUtensorMap q_cached;
+      const int64_t want[5] = {num_heads, seqlen_q, nb, group, dtype};
+      CUresult r = CUDA_SUCCESS;
+      if (q_key_ptr != qb || std::memcmp(q_key, want, sizeof(want)) != 0) {
+        q_key_ptr = nullptr;
+        r = encode(&q_cached, dtype, 4, qb, dims, strides, box);
+        if (r == CUDA_SUCCESS) {
+          q_key_ptr = qb;
+          std::memcpy(q_key, want, sizeof(want));
+        }
+      }
+      maps.q = q_cached;
       if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "Q tensor map encode failed (%d)", (int)r);
     }
     fd::DecodeParams p;
@@ -699,16 +754,8 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
   fd::TensorMaps maps;
   {
     // e4m3 rows: one 128-byte row per (token, KV head)
-    const cuuint64_t dims[4] = {128, (cuuint64_t)num_heads_k, (cuuint64_t)page_block_size,
-                                (cuuint64_t)num_blocks};
-    const cuuint64_t strides[3] = {128, (cuuint64_t)(num_heads_k * 128),
-                                   (cuuint64_t)(page_block_size * num_heads_k * 128)};
-    const cuuint32_t box[4] = {128, 1, (cuuint32_t)chunk, 1};
-    const cuuint32_t box16[4] = {128, 1, 16, 1};
-    CUresult r = encode(&maps.k, FD_DTYPE_E4M3, 4, k_cache, dims, strides, box);
-    if (r == CUDA_SUCCESS) r = encode(&maps.v, FD_DTYPE_E4M3, 4, v_cache, dims, strides, box);
-    if (r == CUDA_SUCCESS) r = encode(&maps.k16, FD_DTYPE_E4M3, 4, k_cache, dims, strides, box16);
-    if (r == CUDA_SUCCESS) r = encode(&maps.v16, FD_DTYPE_E4M3, 4, v_cache, dims, strides, box16);
+    const CUresult r = kv_maps(maps, FD_DTYPE_E4M3, k_cache, v_cache, num_heads_k,
+                               page_block_size, num_blocks, chunk);
     if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "K/V tensor map encode failed (%d)", (int)r);
   }
   const int64_t per_seq_cost =

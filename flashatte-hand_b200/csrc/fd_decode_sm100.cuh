@@ -97,14 +97,20 @@ constexpr int kVProducerWarp = 6;
 // launch epoch, bits [0, 12) the arrivals seen in that epoch.  A counter left
 // by any earlier launch (even one that stopped early) reads as zero, so the
 // workspace never needs clearing.  Returns true for the pair's last arrival.
+// The first arrival of a launch stamps the epoch with one compare-and-swap;
+// every arrival that sees the stamp counts itself with one fetch-and-add, so
+// the tens of CTAs sharing one long sequence's pair, finishing together, do
+// not queue on a compare-and-swap loop.
 __device__ __forceinline__ bool ticket_arrive(uint32_t* t, uint32_t epoch, int nseg) {
-  uint32_t old = atomicAdd(t, 0u);
+  uint32_t cur = *reinterpret_cast<volatile uint32_t*>(t);
   for (;;) {
-    const uint32_t cnt = (old >> 12) == epoch ? (old & 0xFFFu) : 0u;
-    const uint32_t nv = (epoch << 12) | (cnt + 1u);
-    const uint32_t prev = atomicCAS(t, old, nv);
-    if (prev == old) return cnt + 1u == static_cast<uint32_t>(nseg);
-    old = prev;
+    if ((cur >> 12) == epoch) {
+      const uint32_t old = atomicAdd(t, 1u);
+      return (old & 0xFFFu) + 1u == static_cast<uint32_t>(nseg);
+    }
+    const uint32_t prev = atomicCAS(t, cur, (epoch << 12) | 1u);
+    if (prev == cur) return nseg == 1;
+    cur = prev;
   }
 }
 

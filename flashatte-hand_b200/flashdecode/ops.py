@@ -14,6 +14,7 @@ the tensors' device and current stream and raises on any error.
 """
 from __future__ import annotations
 
+import contextlib
 import math
 
 import torch
@@ -27,6 +28,28 @@ _OUT_DTYPES = {torch.bfloat16: FD_DTYPE_BF16, torch.float16: FD_DTYPE_FP16, torc
 
 def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
+
+
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _stream_handle(stream, dev: torch.device) -> int:
+    """cudaStream_t of `stream`, or of the current stream of `dev` (read
+    without building a Stream object when torch offers that)."""
+    if stream is not None:
+        return stream.cuda_stream
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    if _raw_stream is not None:
+        return _raw_stream(idx)
+    return torch.cuda.current_stream(idx).cuda_stream
+
+
+def _on_device(dev: torch.device):
+    """Context that makes `dev` current, or nothing when it already is (the
+    device switch costs more than the rest of a small call)."""
+    if dev.index is None or dev.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(dev)
 
 
 def _require_cuda(*tensors: torch.Tensor) -> None:
@@ -133,38 +156,39 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     ws_ptr, ws_bytes = None, 0
     if workspace is not None:
         ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
-    st = stream if stream is not None else torch.cuda.current_stream(q.device)
+    ctx = _on_device(q.device)
+    sh = _stream_handle(stream, q.device)
     if (k is None) != (v is None):
         raise ValueError("k and v must be given together")
     if kv8:
         if k is not None:
             _check_new_kv(k, v, k_cache, B, q.dtype)
-        with torch.cuda.device(q.device):
+        with ctx:
             status = lib.fd_decode_paged_fp8(
                 _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(k_scale), _ptr(v_scale), _ptr(k),
                 _ptr(v), 0 if k is None else k.shape[1], _ptr(out), _ptr(lse), _ptr(cache_seqlens),
                 _ptr(block_table), int(block_table.shape[1]), B, sq, Hq, Hkv, D, page, num_blocks,
                 _DTYPES[q.dtype], _OUT_DTYPES[odt], scale, 1 if causal else 0,
-                int(max_seqlen_k or 0), ws_ptr, ws_bytes, st.cuda_stream)
+                int(max_seqlen_k or 0), ws_ptr, ws_bytes, sh)
         check(status)
         return (out, lse) if return_softmax_lse else out
     if k is not None:
         _check_new_kv(k, v, k_cache, B)
-        with torch.cuda.device(q.device):
+        with ctx:
             status = lib.fd_decode_paged_kvappend(
                 _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(k), _ptr(v), _ptr(out), _ptr(lse),
                 _ptr(cache_seqlens), _ptr(block_table), int(block_table.shape[1]), B, sq,
                 k.shape[1], Hq, Hkv, D, page, num_blocks, _DTYPES[q.dtype], _OUT_DTYPES[odt],
                 scale, 1 if causal else 0, int(max_seqlen_k or 0), ws_ptr, ws_bytes,
-                st.cuda_stream)
+                sh)
         check(status)
         return (out, lse) if return_softmax_lse else out
-    with torch.cuda.device(q.device):
+    with ctx:
         status = lib.fd_decode_paged_mq(
             _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out), _ptr(lse), _ptr(cache_seqlens),
             _ptr(block_table), int(block_table.shape[1]), B, sq, Hq, Hkv, D, page, num_blocks,
             _DTYPES[q.dtype], _OUT_DTYPES[odt], scale, 1 if causal else 0, int(max_seqlen_k or 0),
-            ws_ptr, ws_bytes, st.cuda_stream)
+            ws_ptr, ws_bytes, sh)
     check(status)
     return (out, lse) if return_softmax_lse else out
 
