@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="budget of the cpu_baseline leg (rank 0, N=1)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--shard", default="auto", choices=["auto", "heads"],
+                    help="N>1: the config's default partition, or KV-head sharding")
     ap.add_argument("--kv", default="native", choices=["native", "fp8"],
                     help="K/V cache storage: the config's dtype, or e4m3 with per-head scales")
     return ap.parse_args()
@@ -217,7 +219,13 @@ def main():
     lib = flashdecode.load_library()
     stream = torch.cuda.current_stream()
     splitter = None
-    if world == 1 or args.config in (1, 2):
+    if world > 1 and args.shard == "heads":
+        # every rank owns Hkv / N KV heads (and their query heads) of every sequence
+        case, _qrange = fdist.head_shard(full, rank, world)
+        scaling, parallel = "strong", f"kvheads{world}"
+        total_kv = full.kv_bytes()
+        t = cases.materialize(case, "cuda", seed=rank)
+    elif world == 1 or args.config in (1, 2):
         # every rank decodes its own full batch: batch sharding of a B*N batch
         case, scaling, parallel = full, "weak", f"dp{world}"
         total_kv = full.kv_bytes() * world

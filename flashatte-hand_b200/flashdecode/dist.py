@@ -7,6 +7,10 @@ partitions are provided here:
 * batch sharding (``batch_shard``): each rank owns whole sequences and their
   KV pages, chosen longest-first (LPT) so skewed length mixes balance.  No
   collective is on the data path; every rank writes its own output rows.
+* KV-head sharding (``head_shard``): each rank owns Hkv / world KV heads of
+  every sequence and the query heads that read them, and holds only those
+  heads' pages; no collective, every rank writes its own output heads.  The
+  natural choice for a small batch of long sequences when Hkv >= world.
 * cross-GPU split-KV (``kv_split_case``): each rank owns a contiguous page
   range of every sequence and decodes it to a normalised fp32 partial
   (O, LSE) per output row; the ranks' partials are merged with LSE weights.
@@ -37,6 +41,28 @@ def batch_shard(case: _cases.DecodeCase, rank: int, world: int):
     if not rows:
         raise ValueError(f"rank {rank} of {world} owns no sequence (batch {case.B})")
     return _cases.subset_case(case, rows, name=f"{case.name}_shard{rank}of{world}"), rows
+
+
+def head_range(num_heads_k: int, rank: int, world: int) -> tuple[int, int]:
+    """KV heads [h0, h1) of `rank`: contiguous, equal shares (Hkv % world == 0)."""
+    if num_heads_k % world != 0:
+        raise ValueError(f"{num_heads_k} KV heads do not split over {world} ranks")
+    per = num_heads_k // world
+    return rank * per, (rank + 1) * per
+
+
+def head_shard(case: _cases.DecodeCase, rank: int, world: int):
+    """(local case with Hkv / world KV heads and Hq / world query heads, the
+    global query-head range [q0, q1) it serves).  Sequences, lengths and the
+    page table are unchanged; the local cache holds only this rank's heads."""
+    h0, h1 = head_range(case.Hkv, rank, world)
+    group = case.Hq // case.Hkv
+    local = _cases.DecodeCase(name=f"{case.name}_heads{rank}of{world}", dtype=case.dtype, B=case.B,
+                              Hq=(h1 - h0) * group, Hkv=h1 - h0, D=case.D, page=case.page,
+                              seqlens=case.seqlens.clone(), block_table=case.block_table.clone(),
+                              num_blocks=case.num_blocks, q_std=case.q_std,
+                              softmax_scale=case.softmax_scale)
+    return local, (h0 * group, h1 * group)
 
 
 def kv_page_range(n_pages: int, rank: int, world: int) -> tuple[int, int]:

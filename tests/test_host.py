@@ -129,3 +129,30 @@ def test_schedule_is_balanced_on_config2():
     st = schedule.split_stats([4096] * 64, 8, 148)
     assert st["tiles_total"] == 64 * 8 * 32
     assert st["tiles_per_cta_max"] - st["tiles_per_cta_min"] <= 2
+
+
+def test_head_shard_slices_heads_and_decodes_the_same_rows():
+    """KV-head sharding: the ranks' KV-head ranges partition the heads, and
+    decoding a rank's head slice (oracle) gives exactly the matching query
+    heads of the full decode."""
+    from flashdecode import dist as fdist
+    from oracle.decode_ref import decode_reference
+    c = cases.custom_case("hs", torch.float32, [37, 0, 200], 8, 4, D=16, page=8, seed=4)
+    t = cases.materialize(c, "cpu", seed=4)
+    full_o, full_l = decode_reference(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"],
+                                      t["block_table"], softmax_scale=c.softmax_scale)
+    world = 2
+    covered = []
+    for rank in range(world):
+        local, (q0, q1) = fdist.head_shard(c, rank, world)
+        h0, h1 = fdist.head_range(c.Hkv, rank, world)
+        covered += list(range(h0, h1))
+        assert local.Hkv == h1 - h0 and local.Hq == q1 - q0 == (h1 - h0) * (c.Hq // c.Hkv)
+        o, l = decode_reference(t["q"][:, :, q0:q1], t["k_cache"][:, :, h0:h1],
+                                t["v_cache"][:, :, h0:h1], local.seqlens, local.block_table,
+                                softmax_scale=local.softmax_scale)
+        assert torch.equal(o, full_o[:, :, q0:q1])
+        assert torch.equal(l, full_l[:, q0:q1])
+    assert covered == list(range(c.Hkv))
+    with pytest.raises(ValueError):
+        fdist.head_range(6, 0, 4)

@@ -1,5 +1,6 @@
 """Multi-GPU decode on one node (NCCL, 2 ranks, one process per GPU): the
-cross-GPU split-KV exchange and batch sharding against the single-GPU result.
+cross-GPU split-KV exchange, batch sharding and KV-head sharding against the
+single-GPU result.
 Skipped when fewer than two GPUs are visible."""
 import datetime
 import os
@@ -74,6 +75,21 @@ def _worker(rank, port, kind, q):
             fin = torch.isfinite(ref_l)
             assert torch.equal(fin, torch.isfinite(lse))
             assert torch.allclose(lse[fin], ref_l[fin], atol=1e-3)
+        elif kind == "heads":
+            local, (q0, q1) = fdist.head_shard(glob, rank, WORLD)
+            h0, h1 = fdist.head_range(glob.Hkv, rank, WORLD)
+            k = t["k_cache"][:, :, h0:h1].contiguous()
+            v = t["v_cache"][:, :, h0:h1].contiguous()
+            out, lse = flashdecode.flash_decode(t["q"][:, :, q0:q1].contiguous(), k, v,
+                                                local.seqlens.cuda(), local.block_table.cuda(),
+                                                return_softmax_lse=True)
+            torch.cuda.synchronize()
+            exp_o, exp_l = ref_o[:, :, q0:q1].float(), ref_l[:, q0:q1]
+            err = (out.float() - exp_o).abs()
+            assert bool((err <= 2e-3 + 1e-2 * exp_o.abs()).all()), float(err.max())
+            fin = torch.isfinite(exp_l)
+            assert torch.equal(fin, torch.isfinite(lse))
+            assert torch.allclose(lse[fin], exp_l[fin], atol=1e-3)
         else:
             sub, rows = fdist.batch_shard(glob, rank, WORLD)
             used = glob.block_table[rows][glob.block_table[rows] >= 0].unique(sorted=True).long().cuda()
@@ -124,3 +140,7 @@ def test_split_kv_over_peer_memory_two_gpus():
 
 def test_batch_shard_across_two_gpus():
     _run("batch")
+
+
+def test_kv_head_shard_across_two_gpus():
+    _run("heads")
