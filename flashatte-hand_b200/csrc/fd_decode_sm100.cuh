@@ -783,49 +783,64 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         for (int i = d; i < nl; i += 128) sl[i] = __ldcg(p.part_lse + sbase * qrows + i);
         named_bar_sync(1, 128);
       }
-      // Segment-outer, row-inner: each step loads one partial value of every
-      // query row (independent loads, several steps in flight), so a pair cut
-      // into many segments merges in a few L2 round trips rather than one per
-      // (segment, row).
+      // A warp covers a 128-dim row with 16-byte loads (lane l: dims 4l..4l+3);
+      // warp w merges rows w, w+4, ...  Each step loads the partial of every
+      // such row for one segment and several steps are in flight, so a pair
+      // cut into tens of segments merges in a few L2 round trips of 16-byte
+      // requests rather than many of 4-byte ones.
       auto lse_of = [&](int j, int h) {
         return staged ? sl[j * qrows + h] : __ldcg(p.part_lse + (sbase + j) * qrows + h);
       };
-      float mx[NCOL], den[NCOL], acc[NCOL];
+      constexpr int kRows = (NCOL + 3) / 4;  // rows per thread
+      const int lane4 = d & 31, rg = d >> 5;
+      float mx[kRows], den[kRows], acc[kRows][4];
 #pragma unroll
-      for (int h = 0; h < NCOL; ++h) {
-        mx[h] = neg_inf;
-        den[h] = 0.f;
-        acc[h] = 0.f;
+      for (int k = 0; k < kRows; ++k) {
+        mx[k] = neg_inf;
+        den[k] = 0.f;
+        acc[k][0] = acc[k][1] = acc[k][2] = acc[k][3] = 0.f;
       }
       for (int j = 0; j < sg.nseg; ++j) {
 #pragma unroll
-        for (int h = 0; h < NCOL; ++h)
-          if (h < qrows) mx[h] = fmaxf(mx[h], lse_of(j, h));
+        for (int k = 0; k < kRows; ++k)
+          if (rg + 4 * k < qrows) mx[k] = fmaxf(mx[k], lse_of(j, rg + 4 * k));
       }
-      const float* po_d = p.part_o + sbase * qrows * kHeadDim + d;
+      const float* po4 = p.part_o + sbase * qrows * kHeadDim + 4 * lane4;
 #pragma unroll 4
       for (int j = 0; j < sg.nseg; ++j) {
-        float o[NCOL];
+        float4 o[kRows];
 #pragma unroll
-        for (int h = 0; h < NCOL; ++h)
-          o[h] = h < qrows ? __ldcg(po_d + (static_cast<int64_t>(j) * qrows + h) * kHeadDim) : 0.f;
+        for (int k = 0; k < kRows; ++k) {
+          const int h = rg + 4 * k;
+          o[k] = h < qrows ? __ldcg(reinterpret_cast<const float4*>(
+                                 po4 + (static_cast<int64_t>(j) * qrows + h) * kHeadDim))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
 #pragma unroll
-        for (int h = 0; h < NCOL; ++h) {
+        for (int k = 0; k < kRows; ++k) {
+          const int h = rg + 4 * k;
           if (h < qrows) {
             const float lj = lse_of(j, h);
-            const float wj = lj == neg_inf ? 0.f : fast_exp2(lj - mx[h]);  // empty parts hold O = 0
-            acc[h] = fmaf(wj, o[h], acc[h]);
-            den[h] += wj;
+            const float wj = lj == neg_inf ? 0.f : fast_exp2(lj - mx[k]);  // empty parts hold O = 0
+            acc[k][0] = fmaf(wj, o[k].x, acc[k][0]);
+            acc[k][1] = fmaf(wj, o[k].y, acc[k][1]);
+            acc[k][2] = fmaf(wj, o[k].z, acc[k][2]);
+            acc[k][3] = fmaf(wj, o[k].w, acc[k][3]);
+            den[k] += wj;
           }
         }
       }
 #pragma unroll
-      for (int h = 0; h < NCOL; ++h) {
+      for (int k = 0; k < kRows; ++k) {
+        const int h = rg + 4 * k;
         if (h < qrows) {
-          put_o(out_index(h), den[h] > 0.f ? acc[h] / den[h] : 0.f);
-          if (d == 0)
+          const float inv = den[k] > 0.f ? 1.f / den[k] : 0.f;
+          const int64_t base = out_index(h) - d + 4 * lane4;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) put_o(base + e, acc[k][e] * inv);
+          if (lane4 == 0)
             put_lse(lse_index(h),
-                    den[h] > 0.f ? (mx[h] + fast_log2(den[h])) * 0.69314718055994531f : neg_inf);
+                    den[k] > 0.f ? (mx[k] + fast_log2(den[k])) * 0.69314718055994531f : neg_inf);
         }
       }
     };
