@@ -144,3 +144,29 @@ def test_fp8_unsupported_shapes_are_refused():
     with pytest.raises(ValueError):
         flashdecode.flash_decode(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"],
                                  t["block_table"])  # scales missing
+
+
+def test_fp8_batch_larger_than_one_launch():
+    """More than 512 sequences: the query parts are split per launch chunk
+    into the same workspace region, one chunk after the other."""
+    lens = [37 + (i * 53) % 700 for i in range(1200)]
+    c = cases.custom_case("fp8_big", torch.bfloat16, lens, 32, 8, page=16, seed=9)
+    t = cases.materialize_e4m3(c, "cuda", seed=9)
+    out, lse = run(t, c)
+    torch.cuda.synchronize()
+    rows = [0, 1, 511, 512, 513, 1023, 1024, 1199]
+    ref_o, ref_l = oracle(t, c, rows=rows)
+    check(out, lse, ref_o, ref_l, rows=rows)
+
+
+@pytest.mark.parametrize("sq", [2, 3])
+def test_fp8_multi_token_causal_page16(sq):
+    c = cases.custom_case(f"fp8_mq16_{sq}", torch.float16, [5, 16, 17, 900, 0, 2001], 16, 8,
+                          page=16, seed=20 + sq)
+    t = cases.materialize_e4m3(c, "cuda", seed=20 + sq)
+    g = torch.Generator(device="cuda").manual_seed(sq)
+    t["q"] = torch.randn((c.B, sq, 16, 128), generator=g, device="cuda", dtype=torch.float16)
+    out, lse = run(t, c, causal=True)
+    torch.cuda.synchronize()
+    ref_o, ref_l = oracle(t, c, causal=True)
+    check(out, lse, ref_o, ref_l)
