@@ -397,7 +397,7 @@ def main():
                    "Hq": full.Hq, "Hkv": full.Hkv, "head_dim": full.D, "page": full.page,
                    "l2": "inputs larger than L2 (KV cache > 126 MB), no flush"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-        "gpu_launches": (launches_per_call + (1 if fp8 else 0)) * args.steps, "clocks": clk.summary(),
+        "gpu_launches": launches_per_call * args.steps, "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
 

@@ -663,23 +663,10 @@ int fd_decode_paged_kvappend(const void* q, void* k_cache, void* v_cache, const 
                      nullptr);
 }
 
-// e4m3 K/V cache (see fd_decode_paged_fp8 in the header).  Per launch of at
-// most kMaxBatchPerLaunch sequences: split the query rows into e4m3 parts
-// (fd_qsplit.cu) into the workspace, then run the e4m3 tensor-core kernel.
-struct Kv8Layout {
-  fd::WorkspaceLayout base;
-  size_t q8_off, qinv_off, total;
-};
-static Kv8Layout kv8_layout(int64_t nb_max, int64_t num_heads_k, int64_t qrows, int sms) {
-  auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
-  Kv8Layout l;
-  l.base = fd::workspace_layout(nb_max, num_heads_k, qrows, sms);
-  const size_t pairs = static_cast<size_t>(nb_max * num_heads_k);
-  l.q8_off = up(l.base.total);
-  l.qinv_off = l.q8_off + up(pairs * 3 * fd::kMaxGroup * fd::kHeadDim);
-  l.total = l.qinv_off + up(pairs * fd::kMaxGroup * 4);
-  return l;
-}
+// e4m3 K/V cache (see fd_decode_paged_fp8 in the header): one launch of the
+// e4m3 tensor-core kernel per kMaxBatchPerLaunch sequences; the kernel splits
+// the 16-bit query rows into e4m3 parts itself.  Same workspace as the
+// 16-bit path.
 
 static int check_kv8_args(const void* q, const void* k_cache, const void* v_cache,
                           const float* k_scale, const float* v_scale, const void* out,
@@ -737,7 +724,7 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
   const int sms = device_sms(dev);
   if (sms <= 0) return set_error(FD_ERR_CUDA, "cannot query SM count");
   const int64_t nb_max = batch_size < fd::kMaxBatchPerLaunch ? batch_size : fd::kMaxBatchPerLaunch;
-  const Kv8Layout wl = kv8_layout(nb_max, num_heads_k, qrows, sms);
+  const fd::WorkspaceLayout wl = fd::workspace_layout(nb_max, num_heads_k, qrows, sms);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (ws == nullptr) {
     ws = static_cast<uint8_t*>(internal_workspace(dev, wl.total, st));
@@ -765,23 +752,10 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
   int64_t per_launch = INT32_MAX / per_seq_cost;
   if (per_launch > fd::kMaxBatchPerLaunch) per_launch = fd::kMaxBatchPerLaunch;
   const int es = esize(q_dtype);
-  uint8_t* q8 = ws + wl.q8_off;
-  float* q_inv = reinterpret_cast<float*>(ws + wl.qinv_off);
+  std::memset(&maps.q, 0, sizeof(maps.q));  // the e4m3 kernel reads the query through p.q
   for (int64_t b0 = 0; b0 < batch_size; b0 += per_launch) {
     const int64_t nb = batch_size - b0 < per_launch ? batch_size - b0 : per_launch;
     const uint8_t* qb = static_cast<const uint8_t*>(q) + b0 * seqlen_q * num_heads * 128 * es;
-    cudaError_t e = fd::launch_split_query(qb, q_dtype, static_cast<int>(nb),
-                                           static_cast<int>(seqlen_q), static_cast<int>(num_heads),
-                                           static_cast<int>(num_heads_k), q8, q_inv, st);
-    if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "query split launch: %s", cudaGetErrorString(e));
-    {
-      // [nb * Hkv] blocks of 48 rows x 128 bytes, one box per (sequence, KV head)
-      const cuuint64_t dims[3] = {128, 3 * fd::kMaxGroup, (cuuint64_t)(nb * num_heads_k)};
-      const cuuint64_t strides[2] = {128, 3 * fd::kMaxGroup * 128};
-      const cuuint32_t box[3] = {128, 3 * fd::kMaxGroup, 1};
-      const CUresult r = encode(&maps.q, FD_DTYPE_E4M3, 3, q8, dims, strides, box);
-      if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "query-part tensor map encode failed (%d)", (int)r);
-    }
     fd::DecodeParams p{};
     p.out = static_cast<uint8_t*>(out) + b0 * seqlen_q * num_heads * 128 * esize(out_dtype);
     p.lse = lse != nullptr ? lse + b0 * num_heads * seqlen_q : nullptr;
@@ -798,10 +772,10 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
     p.page = static_cast<int>(page_block_size);
     p.chunk = chunk;
     p.scale_log2 = softmax_scale * 1.4426950408889634f;
-    p.err = reinterpret_cast<int*>(ws + wl.base.err_off);
-    p.tickets = reinterpret_cast<uint32_t*>(ws + wl.base.tickets_off);
-    p.part_lse = reinterpret_cast<float*>(ws + wl.base.lse_off);
-    p.part_o = reinterpret_cast<float*>(ws + wl.base.o_off);
+    p.err = reinterpret_cast<int*>(ws + wl.err_off);
+    p.tickets = reinterpret_cast<uint32_t*>(ws + wl.tickets_off);
+    p.part_lse = reinterpret_cast<float*>(ws + wl.lse_off);
+    p.part_o = reinterpret_cast<float*>(ws + wl.o_off);
     p.timeout_ns = timeout_ns();
     p.epoch = next_epoch();
     p.cost_tile = cost_tile();
@@ -811,10 +785,10 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
     p.len_add = len_add;
     p.k_scale = k_scale;
     p.v_scale = v_scale;
-    p.q_inv = q_inv;
+    p.q = qb;
     const int64_t work_bound = nb * num_heads_k * tiles_bound;
     const int grid = static_cast<int>(work_bound < sms ? work_bound : sms);
-    e = fd::launch_decode_sm100_kv8(maps, p, q_dtype, out_dtype == FD_DTYPE_FP32, grid, st);
+    const cudaError_t e = fd::launch_decode_sm100_kv8(maps, p, q_dtype, out_dtype == FD_DTYPE_FP32, grid, st);
     if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "sm100 e4m3 launch: %s", cudaGetErrorString(e));
   }
   return set_ok();
@@ -830,7 +804,7 @@ size_t fd_decode_workspace_size_fp8(int64_t batch_size, int64_t seqlen_q, int64_
   const int sms = device_sms(dev);
   if (sms <= 0) return 0;
   const int64_t nb = batch_size < fd::kMaxBatchPerLaunch ? batch_size : fd::kMaxBatchPerLaunch;
-  return kv8_layout(nb, num_heads_k, seqlen_q * (num_heads / num_heads_k), sms).total;
+  return fd::workspace_layout(nb, num_heads_k, seqlen_q * (num_heads / num_heads_k), sms).total;
 }
 
 int fd_append_kv_paged_fp8(const void* k_new, const void* v_new, void* k_cache, void* v_cache,

@@ -68,16 +68,28 @@ template <bool KV8> struct Geo {
   static constexpr int kOCols = KV8 ? 3 * kMaxGroup : 2 * kMaxGroup;  // of one O^T tile
   static constexpr int kSBufs = 3;
   static constexpr int kTmemCols = KV8 ? 256 : 128;
-  // kfull/kempty/vfull/vempty per stage, s_full/s_empty per S buffer, p_full/o_full x2
-  static constexpr int kNumBars = 4 * kStages + 2 * kSBufs + 4;
+  // e4m3: inverse query-row scales, one slot per segment, from the K producer
+  // to the softmax warps (q_full barrier per slot).  The producer runs at most
+  // kStages + kSBufs tiles ahead of the softmax, so 16 slots never overrun.
+  static constexpr int kQRing = KV8 ? 16 : 0;
+  static_assert(kQRing == 0 || kQRing > kStages + kSBufs, "query-scale ring too short");
+  // e4m3: the 16-bit query rows of a segment (16 x 256 B), fetched one
+  // segment ahead by a bulk copy into one of two buffers
+  static constexpr int kQRawBufs = KV8 ? 2 : 0;
+  static constexpr int kQRawBytes = kMaxGroup * kHeadDim * 2;
+  // kfull/kempty/vfull/vempty per stage, s_full/s_empty per S buffer,
+  // p_full/o_full x2, q_full per query-scale slot, qraw_full per raw buffer
+  static constexpr int kNumBars = 4 * kStages + 2 * kSBufs + 4 + kQRing + kQRawBufs;
   // Shared-memory carve-up, offsets from a 1024-byte aligned base.
   static constexpr int kOffStages = 0;
   static constexpr int kOffP = kOffStages + kStages * kStageBytes;
-  static constexpr int kOffBars = kOffP + 2 * kPBufBytes;
+  static constexpr int kOffQRaw = kOffP + 2 * kPBufBytes;
+  static constexpr int kOffBars = kOffQRaw + kQRawBufs * kQRawBytes;
   static constexpr int kOffMisc = kOffBars + kNumBars * 8;           // tmem slot, abort, last flag
   static constexpr int kOffRed = (kOffMisc + 64 + 15) & ~15;         // [2][4][16] floats tile maxima
   static constexpr int kOffFin = kOffRed + 2 * 4 * kMaxGroup * 4;    // [2][4][16] floats row sums
-  static constexpr int kOffPrefix = kOffFin + 2 * 4 * kMaxGroup * 4; // [B+1] pair-cost prefix sums
+  static constexpr int kOffQInv = kOffFin + 2 * 4 * kMaxGroup * 4;   // [kQRing][16] floats
+  static constexpr int kOffPrefix = kOffQInv + kQRing * kMaxGroup * 4;  // [B+1] pair-cost prefix sums
   static constexpr int kOffLens = kOffPrefix + (kMaxBatchPerLaunch + 1) * 4;  // [B] clamped lengths
   static constexpr int kSmemUsed = kOffLens + kMaxBatchPerLaunch * 4;
   static constexpr int kSmemBytes = kSmemUsed + 1024;                // slack for 1024-B alignment
@@ -151,6 +163,9 @@ __host__ __device__ constexpr uint32_t make_idesc_e4m3(bool a_mn_major, bool b_m
 template <typename T> struct DType;
 template <> struct DType<__nv_bfloat16> {
   static constexpr bool kBf16 = true;
+  static __device__ __forceinline__ float2 unpack2(uint32_t w) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+  }
   static __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
     const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     const float2 hf = __bfloat1622float2(h);
@@ -161,6 +176,9 @@ template <> struct DType<__nv_bfloat16> {
 };
 template <> struct DType<__half> {
   static constexpr bool kBf16 = false;
+  static __device__ __forceinline__ float2 unpack2(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+  }
   static __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
     const __half2 h = __floats2half2_rn(a, b);
     const float2 hf = __half22float2(h);
@@ -295,6 +313,102 @@ struct Schedule {
   }
 };
 
+// ---------------------------------------------------------------- e4m3 query
+// With an e4m3 K cache the QK product runs as kind::f8f6f4 UMMAs, whose
+// operands must both be 8-bit.  Each 16-bit query row is scaled by a power of
+// two 2^k that brings its largest magnitude into [128, 256) (below the e4m3
+// maximum 448) and split into three e4m3 parts x = p0 + p1/16 + p2/256
+// (fd_fp8.cuh); the kernel multiplies the parts side by side, recombines S in
+// fp32 and undoes 2^k exactly.  The K producer warp does this once per
+// segment for the NCOL rows the kernel reads (r = qi * group + g): lane l
+// holds row r = l / (32 / NCOL), 4 NCOL dims from 4 NCOL (l % (32 / NCOL)).
+template <int NCOL> struct QuerySplitMap {
+  static constexpr int kLanesPerRow = 32 / NCOL;         // 8, 4, 2
+  static constexpr int kDims = kHeadDim / kLanesPerRow;  // 16, 32, 64
+  static constexpr int kChunks = kDims / 16;             // 16-dim e4m3 chunks per part
+  static constexpr int kRaw = kDims / 8;                 // 16-byte pieces of the 16-bit row
+};
+
+// Lane 0: bulk-copy the segment's query rows r = qi * group + g (256 B each)
+// into `dst` (row r at r * 256), completing on `bar`.  The group's rows of one
+// query token are adjacent heads, so one copy per token.
+template <typename T, bool MULTI>
+__device__ __forceinline__ void fetch_query_rows(const DecodeParams& p, int b, int kvh, int qrows,
+                                                 uint8_t* dst, uint64_t* bar) {
+  const int sq = MULTI ? p.seqlen_q : 1;
+  const uint32_t row_bytes = kHeadDim * 2;
+  mbar_arrive_expect_tx(bar, static_cast<uint32_t>(qrows) * row_bytes);
+  const T* base = static_cast<const T*>(p.q) +
+                  (static_cast<int64_t>(b) * sq * p.num_heads + kvh * p.group) * kHeadDim;
+  for (int qi = 0; qi < sq; ++qi)
+    bulk_load(dst + qi * p.group * row_bytes, base + static_cast<int64_t>(qi) * p.num_heads * kHeadDim,
+              p.group * row_bytes, bar);
+}
+
+// The lane's 4 NCOL query values from the staged rows, zeros for rows
+// r >= qrows.
+template <int NCOL>
+__device__ __forceinline__ void read_query_rows(const uint8_t* rows, int qrows, int lane,
+                                                uint4 (&raw)[QuerySplitMap<NCOL>::kRaw]) {
+  using M = QuerySplitMap<NCOL>;
+  const int r = lane / M::kLanesPerRow, sub = lane % M::kLanesPerRow;
+  const uint4* src = reinterpret_cast<const uint4*>(rows + r * (kHeadDim * 2) + sub * (M::kDims * 2));
+#pragma unroll
+  for (int i = 0; i < M::kRaw; ++i) raw[i] = r < qrows ? src[i] : make_uint4(0, 0, 0, 0);
+}
+
+template <typename T> __device__ __forceinline__ void unpack8(const uint4& w, float2 (&f)[4]) {
+  f[0] = DType<T>::unpack2(w.x);
+  f[1] = DType<T>::unpack2(w.y);
+  f[2] = DType<T>::unpack2(w.z);
+  f[3] = DType<T>::unpack2(w.w);
+}
+
+// Scale and split the lane's values (all 32 lanes call this together):
+// part[j][k] = part k of the lane's dims 16 j .. 16 j + 15.  Returns 2^-k,
+// the inverse of the row's scale.
+template <typename T, int NCOL>
+__device__ __forceinline__ float split_query_rows(const uint4 (&raw)[QuerySplitMap<NCOL>::kRaw],
+                                                  uint4 (&part)[QuerySplitMap<NCOL>::kChunks][3]) {
+  using M = QuerySplitMap<NCOL>;
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < M::kRaw; ++i) {
+    float2 f[4];
+    unpack8<T>(raw[i], f);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) mx = fmaxf(mx, fmaxf(fabsf(f[e].x), fabsf(f[e].y)));
+  }
+#pragma unroll
+  for (int o = 1; o < M::kLanesPerRow; o <<= 1)  // the row's other lanes (adjacent)
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  // 2^k with mx 2^k in [128, 256): k = 7 - floor(log2 mx), clamped to the
+  // normal range; rows of zeros keep k = 0.
+  int k = 0;
+  if (mx > 0.f && mx <= 3.0e38f) {
+    const int e = ((__float_as_int(mx) >> 23) & 0xff) - 127;
+    k = 7 - e;
+    k = k < -126 ? -126 : (k > 126 ? 126 : k);
+  }
+  const float sc = __int_as_float((k + 127) << 23);
+#pragma unroll
+  for (int j = 0; j < M::kChunks; ++j) {
+    float x[16];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float2 f[4];
+      unpack8<T>(raw[2 * j + h], f);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        x[8 * h + 2 * e] = f[e].x * sc;
+        x[8 * h + 2 * e + 1] = f[e].y * sc;
+      }
+    }
+    e4m3_split16(x, part[j]);
+  }
+  return __int_as_float((127 - k) << 23);
+}
+
 __device__ __forceinline__ bool lane0_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                            uint64_t budget, int lane) {
   int ok = 1;
@@ -338,6 +452,9 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   uint64_t* s_empty = s_full + G::kSBufs;    // [G::kSBufs] S^T read by the softmax warps
   uint64_t* p_full = s_empty + G::kSBufs;    // [2] P written
   uint64_t* o_full = p_full + 2;          // [2] O^T in TMEM
+  uint64_t* q_full = o_full + 2;          // [G::kQRing] inverse query-row scales written
+  uint64_t* qraw_full = q_full + G::kQRing;  // [G::kQRawBufs] raw query rows landed
+  uint8_t* qraw_buf = smem + G::kOffQRaw;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + G::kOffMisc + 4);
   volatile int* last_flag = reinterpret_cast<volatile int*>(smem + G::kOffMisc + 8);
@@ -345,6 +462,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   volatile int* tiles_total = reinterpret_cast<volatile int*>(smem + G::kOffMisc + 12);
   float* red = reinterpret_cast<float*>(smem + G::kOffRed);
   float* fin = reinterpret_cast<float*>(smem + G::kOffFin);
+  float* qinv_ring = reinterpret_cast<float*>(smem + G::kOffQInv);
   int* prefix = reinterpret_cast<int*>(smem + G::kOffPrefix);
   int* lens = reinterpret_cast<int*>(smem + G::kOffLens);
 
@@ -379,6 +497,8 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       mbar_init(&p_full[i], 128);
       mbar_init(&o_full[i], 1);
     }
+    for (int i = 0; i < G::kQRing; ++i) mbar_init(&q_full[i], 1);
+    for (int i = 0; i < G::kQRawBufs; ++i) mbar_init(&qraw_full[i], 1);
     *abort_flag = 0;
     *last_flag = 0;
     *tiles_total = 0x7fffffff;
@@ -460,7 +580,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         tma_prefetch_desc(&tm_v);
         tma_prefetch_desc(&tm_v16);
       } else {
-        tma_prefetch_desc(&tm_q);
+        if constexpr (!KV8) tma_prefetch_desc(&tm_q);  // e4m3: no query map
         tma_prefetch_desc(&tm_k);
         tma_prefetch_desc(&tm_k16);
       }
@@ -470,9 +590,9 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     const CUtensorMap* map_full = is_v ? &tm_v : &tm_k;
     const CUtensorMap* map_tail = is_v ? &tm_v16 : &tm_k16;
     const int operand_off = is_v ? G::kOperandBytes : 0;
-    // query rows ride with K: 16-bit rows (two halves of qrows x 128 B), or
-    // the 48 x 128 B block of e4m3 query parts
-    const uint32_t extra_tx = is_v ? 0u : (KV8 ? static_cast<uint32_t>(G::kQSlotBytes) : 2u * qrows * 128u);
+    // 16-bit query rows ride with K (two halves of qrows x 128 B); the e4m3
+    // query parts are stored into the stage by this warp instead
+    const uint32_t extra_tx = (is_v || KV8) ? 0u : 2u * qrows * 128u;
     constexpr uint32_t kRowTx = KV8 ? 128u : 256u;  // K or V bytes per token
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_keep = policy_evict_last();
@@ -481,7 +601,39 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     int64_t it = 0;
     bool ok = true;
     Segment s;
-    for (bool have = sched.first(cta, s); have && ok; have = sched.next(s, range_end, s)) {
+    bool have = sched.first(cta, s);
+    // e4m3 (warp 0): the segment's 16-bit query rows, bulk-copied one
+    // segment ahead into qraw_buf, and their e4m3 parts (split_query_rows).
+    using QM = QuerySplitMap<NCOL>;
+    [[maybe_unused]] uint4 qpart[QM::kChunks][3];
+    if constexpr (KV8) {
+      if (!is_v && have && lane == 0) fetch_query_rows<T, MULTI>(p, s.b, s.kvh, qrows, qraw_buf, &qraw_full[0]);
+    }
+    for (int64_t sgo = 0; have && ok; ++sgo) {
+      Segment nx;
+      const bool have_nx = sched.next(s, range_end, nx);
+      if constexpr (KV8) {
+        if (!is_v) {
+          const int rb = static_cast<int>(sgo & 1);
+          ok = mbar_wait_bounded(&qraw_full[rb], static_cast<uint32_t>((sgo >> 1) & 1), abort_flag, budget);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          uint4 qraw[QM::kRaw];
+          read_query_rows<NCOL>(qraw_buf + rb * G::kQRawBytes, qrows, lane, qraw);
+          const float qinv = split_query_rows<T, NCOL>(qraw, qpart);
+          __syncwarp();  // buffer rb ^ 1 was read a segment ago; refill it
+          if (have_nx && lane == 0)
+            fetch_query_rows<T, MULTI>(p, nx.b, nx.kvh, qrows, qraw_buf + (rb ^ 1) * G::kQRawBytes,
+                                       &qraw_full[rb ^ 1]);
+          // Slot sgo % kQRing was last read by the softmax warps for segment
+          // sgo - kQRing, which began more than kStages + kSBufs tiles ago.
+          const int slot = static_cast<int>(sgo % G::kQRing);
+          const int qr = lane / QM::kLanesPerRow;
+          if (lane % QM::kLanesPerRow == 0) qinv_ring[slot * kMaxGroup + qr] = qr < qrows ? qinv : 0.f;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&q_full[slot]);
+        }
+      }
       const int32_t* bt_row = p.block_table + static_cast<int64_t>(s.b) * p.bt_stride;
       for (int t = 0; t < s.ntiles; ++t, ++it) {
         const int tok0 = (s.tile0 + t) * kTileTokens;
@@ -500,14 +652,35 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
                         abort_flag, budget, lane);
         if (!ok) break;
         uint8_t* sdst = stages + stage * G::kStageBytes;
+        if constexpr (KV8) {
+          // A stage already holds this segment's query parts unless its
+          // previous tile (it - kStages) belonged to an earlier segment.
+          if (!is_v && t < G::kStages) {
+            // The query parts, as rows part * 16 + r of 128 B laid out as a
+            // 128B-swizzled TMA box would leave them: 16-byte chunk c of row R
+            // at chunk c ^ (R & 7).  Rows r >= NCOL are never read back from
+            // S.  Ordered before the `full` arrival below.
+            uint8_t* qdst = sdst + 2 * G::kOperandBytes;
+            const int r = lane / QM::kLanesPerRow, sub = lane % QM::kLanesPerRow;
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+              const int row = k * kMaxGroup + r;
+#pragma unroll
+              for (int j = 0; j < QM::kChunks; ++j) {
+                const int c = sub * QM::kChunks + j;
+                *reinterpret_cast<uint4*>(qdst + row * 128 + ((c ^ (row & 7)) << 4)) = qpart[j][k];
+              }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+          }
+        }
         if (lane == 0) {
           mbar_arrive_expect_tx(&ring_full[stage], static_cast<uint32_t>(nbox * box) * kRowTx + extra_tx);
-          if (!is_v) {
-            uint8_t* qdst = sdst + 2 * G::kOperandBytes;
-            if constexpr (KV8) {
-              tma_load_3d(&tm_q, &ring_full[stage], qdst, 0, 0, s.b * hkv + s.kvh, pol_keep);
-            } else {
+          if constexpr (!KV8) {
+            if (!is_v) {
               // rows qi * group + g: query token qi, head kvh * group + g
+              uint8_t* qdst = sdst + 2 * G::kOperandBytes;
               tma_load_4d(&tm_q, &ring_full[stage], qdst, 0, s.kvh * group, 0, s.b, pol_keep);
               tma_load_4d(&tm_q, &ring_full[stage], qdst + G::kQSlotBytes / 2, 64, s.kvh * group, 0,
                           s.b, pol_keep);
@@ -525,6 +698,8 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         }
         __syncwarp();
       }
+      s = nx;
+      have = have_nx;
     }
     if (!is_v && lane == 0) *tiles_total = static_cast<int>(it);
   } else if (warp == 1 || warp == kQkWarp) {
@@ -860,6 +1035,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     Segment seg{}, prev_seg{};
     int t = 0;
     int64_t it = 0;
+    int64_t sgo = 0;  // segment ordinal (slot of the query-scale ring)
     for (bool have = sched.first(cta, seg); have; ++it, ++t) {
       bool prev_open = false;
       if (t == seg.ntiles) {  // next segment, if the range has one
@@ -867,6 +1043,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         if (!sched.next(seg, range_end, nx)) break;
         prev_seg = seg;
         seg = nx;
+        ++sgo;
         t = 0;
         prev = cur;
         reset(cur);
@@ -875,9 +1052,11 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       if constexpr (KV8) {
         if (t == 0) {
           const float ks = __ldg(p.k_scale + seg.kvh) * p.scale_log2;
-          const float* qi = p.q_inv + (static_cast<int64_t>(seg.b) * hkv + seg.kvh) * kMaxGroup;
+          const int slot = static_cast<int>(sgo % G::kQRing);
+          mbar_wait_bounded(&q_full[slot], static_cast<uint32_t>((sgo / G::kQRing) & 1), abort_flag, budget);
+          const float* qi = qinv_ring + slot * kMaxGroup;
 #pragma unroll
-          for (int h = 0; h < NCOL; ++h) qf[h] = ks * __ldg(qi + h);
+          for (int h = 0; h < NCOL; ++h) qf[h] = ks * qi[h];
         }
       }
       // ---- softmax of tile `it`

@@ -48,11 +48,11 @@ struct DecodeParams {
   int cost_tile, cost_seg;    // split cost model: fixed cost per tile and per pair, in
                               // units where a full tile's K/V bytes cost 8
   // e4m3 K/V only: dequantisation scales per KV head (K = k8 * k_scale[h],
-  // V = v8 * v_scale[h]) and, per (sequence, KV head, query row), the
-  // inverse of the power-of-two scale the query row was split with.
+  // V = v8 * v_scale[h]) and the 16-bit query [B, seqlen_q, Hq, 128], which
+  // the kernel splits into e4m3 parts itself.
   const float* k_scale;
   const float* v_scale;
-  const float* q_inv;         // [batch * num_heads_k * 16]
+  const void* q;
 };
 
 struct SimtParams {
@@ -103,20 +103,12 @@ cudaError_t launch_sm100_bf16(const TensorMaps& m, const DecodeParams& p, int gr
 cudaError_t launch_sm100_bf16_f32(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
 cudaError_t launch_sm100_fp16(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
 cudaError_t launch_sm100_fp16_f32(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
-// e4m3 K/V cache, query of type bf16 / fp16 (tm.q then maps the pre-split
-// e4m3 query parts, see launch_split_query), output of the query type or fp32.
+// e4m3 K/V cache, query of type bf16 / fp16 (read through DecodeParams::q;
+// tm.q is not used), output of the query type or fp32.
 cudaError_t launch_sm100_kv8_bf16(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
 cudaError_t launch_sm100_kv8_bf16_f32(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
 cudaError_t launch_sm100_kv8_fp16(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
 cudaError_t launch_sm100_kv8_fp16_f32(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream);
-
-// Split every query row of q [B, sq, Hq, 128] (16-bit, dtype 0 = bf16,
-// 1 = fp16) into three e4m3 parts for the e4m3-cache kernel: for each
-// (sequence, KV head) a 48 x 128-byte block (rows part * 16 + r, r = qi *
-// group + g; rows r >= qrows zero) in q8 [B * Hkv, 48, 128], and the inverse
-// of each row's power-of-two scale in q_inv [B * Hkv, 16].
-cudaError_t launch_split_query(const void* q, int dtype, int batch, int seqlen_q, int num_heads,
-                               int num_heads_k, uint8_t* q8, float* q_inv, cudaStream_t stream);
 
 // Launchers.  dtype: 0 bf16, 1 fp16; out_fp32 selects an fp32 output.
 cudaError_t launch_decode_sm100(const TensorMaps& m, const DecodeParams& p, int dtype,
