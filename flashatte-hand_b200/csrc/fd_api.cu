@@ -16,7 +16,6 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
-#include <atomic>
 #include <mutex>
 
 #include "../../include/flashdecode.h"
@@ -189,14 +188,6 @@ CUresult kv_maps(fd::TensorMaps& m, int dtype, const void* k, const void* v, int
   m.k16 = cached[2];
   m.v16 = cached[3];
   return CUDA_SUCCESS;
-}
-
-// Launch epoch for the split-pair arrival counters: consecutive launches get
-// different values in 1 .. 2^20-1 (0 never occurs, so a zeroed workspace
-// reads as "no arrivals").
-uint32_t next_epoch() {
-  static std::atomic<uint32_t> counter{0};
-  return counter.fetch_add(1, std::memory_order_relaxed) % 0xFFFFFu + 1u;
 }
 
 // Split cost model (units: a full tile's K/V bytes = 8): fixed cost per
@@ -455,7 +446,7 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
     p.part_lse = reinterpret_cast<float*>(ws + wl.lse_off);
     p.part_o = reinterpret_cast<float*>(ws + wl.o_off);
     p.timeout_ns = timeout_ns();
-    p.epoch = next_epoch();
+    p.epoch_word = reinterpret_cast<uint32_t*>(ws + wl.epoch_off);
     p.cost_tile = cost_tile();
     p.cost_seg = cost_seg();
     p.xworld = 0;
@@ -777,7 +768,7 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
     p.part_lse = reinterpret_cast<float*>(ws + wl.lse_off);
     p.part_o = reinterpret_cast<float*>(ws + wl.o_off);
     p.timeout_ns = timeout_ns();
-    p.epoch = next_epoch();
+    p.epoch_word = reinterpret_cast<uint32_t*>(ws + wl.epoch_off);
     p.cost_tile = cost_tile();
     p.cost_seg = cost_seg();
     p.xworld = 0;

@@ -15,6 +15,7 @@ WorkspaceLayout workspace_layout(int64_t batch_per_launch, int64_t num_heads_k, 
   const size_t slots = pairs + static_cast<size_t>(grid_max);
   WorkspaceLayout w;
   w.err_off = 0;
+  w.epoch_off = 64;  // two words, see DecodeParams::epoch_word
   w.done_off = 128;
   w.tickets_off = 256;
   w.lse_off = w.tickets_off + up(pairs * 4);

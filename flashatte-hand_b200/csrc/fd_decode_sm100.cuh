@@ -460,6 +460,8 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   volatile int* last_flag = reinterpret_cast<volatile int*>(smem + G::kOffMisc + 8);
   // Tiles of this CTA, published by the producer once its walk is done.
   volatile int* tiles_total = reinterpret_cast<volatile int*>(smem + G::kOffMisc + 12);
+  // This launch's epoch (see DecodeParams::epoch_word), read once by thread 0.
+  uint32_t* launch_epoch = reinterpret_cast<uint32_t*>(smem + G::kOffMisc + 16);
   float* red = reinterpret_cast<float*>(smem + G::kOffRed);
   float* fin = reinterpret_cast<float*>(smem + G::kOffFin);
   float* qinv_ring = reinterpret_cast<float*>(smem + G::kOffQInv);
@@ -517,6 +519,10 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   }
   const CostModel cm{p.cost_tile, p.cost_seg};
   pdl_wait_prerequisites();
+  // The epoch load is issued here and consumed after the sequence lengths'
+  // loads, so the two round trips overlap.
+  uint32_t epoch_ld = 0;
+  if (tid == 0) epoch_ld = *reinterpret_cast<volatile uint32_t*>(p.epoch_word);
   for (int b = tid; b < batch; b += kSm100Threads) {
     const int stored = __ldg(p.seqlens + b);
     // keys cached before this step plus the ones it appended
@@ -526,7 +532,10 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     lens[b] = len;
     prefix[b + 1] = cm.pair_cost(len);
   }
-  if (tid == 0) prefix[0] = 0;
+  if (tid == 0) {
+    prefix[0] = 0;
+    *launch_epoch = epoch_ld & 0xFFFFFu;
+  }
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -701,7 +710,17 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       s = nx;
       have = have_nx;
     }
-    if (!is_v && lane == 0) *tiles_total = static_cast<int>(it);
+    if (!is_v && lane == 0) {
+      *tiles_total = static_cast<int>(it);
+      // Every CTA has read this launch's epoch before it counts itself here;
+      // the last to count hands the next launch a new one (1 .. 2^20-1; a
+      // zeroed workspace starts at 0, consistent with its zeroed counters),
+      // which that launch reads only after this grid has completed.  Done
+      // after the last load is issued, the round trips overlap the drain of
+      // the ring, and CTAs arrive spread over their different finishing times.
+      const uint32_t e = *launch_epoch;
+      if (ticket_arrive(p.epoch_word + 1, e, static_cast<int>(gridDim.x))) p.epoch_word[0] = e % 0xFFFFFu + 1u;
+    }
   } else if (warp == 1 || warp == kQkWarp) {
     // ---------------------------------------------------------- UMMA issuers
     // A tcgen05.mma of M = 128, K = 16 occupies the tensor pipe ~48 cycles
@@ -939,7 +958,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       named_bar_sync(1, 128);
       if (d == 0) {
         int is_last = 0;
-        if (!*abort_flag) is_last = ticket_arrive(p.tickets + sg.pair, p.epoch, sg.nseg) ? 1 : 0;
+        if (!*abort_flag) is_last = ticket_arrive(p.tickets + sg.pair, *launch_epoch, sg.nseg) ? 1 : 0;
         *last_flag = is_last;
       }
       named_bar_sync(1, 128);

@@ -32,7 +32,11 @@ struct DecodeParams {
   uint32_t* tickets;          // [batch * num_heads_k] epoch-tagged arrival counters
   int* err;                   // device error word
   unsigned long long timeout_ns;
-  uint32_t epoch;             // 1 .. 2^20-1, different for consecutive launches
+  // Launch epoch kept on the device (workspace): [0] the epoch the next
+  // launch uses, [1] the launch's epoch-tagged count of CTAs that have read
+  // it; the last of them advances [0].  A launch replayed from a CUDA graph
+  // therefore gets a fresh epoch like any other launch.
+  uint32_t* epoch_word;
   // Cross-GPU split-KV exchange (xworld > 0): instead of out/lse, every
   // result row goes as fp32 O and ln-LSE to each rank's exchange part
   // xpart[j] (O at [row*128 + d], LSE at [xlse_off + lse row]); the CTA that
@@ -86,7 +90,7 @@ cudaError_t launch_append_kv_e4m3(const AppendParams& p, int src_dtype, cudaStre
 
 // Workspace carve-up for the tensor-core kernel.
 struct WorkspaceLayout {
-  size_t err_off, done_off, tickets_off, lse_off, o_off, total;
+  size_t err_off, epoch_off, done_off, tickets_off, lse_off, o_off, total;
 };
 WorkspaceLayout workspace_layout(int64_t batch_per_launch, int64_t num_heads_k, int64_t qrows,
                                  int grid_max);

@@ -78,8 +78,10 @@ void run_kernel(const void* q, const void* k_cache_paged, const void* v_cache_pa
  * max_seqlen_k: upper bound on cache_seqlens (0 = unknown); only sizes the grid.
  * workspace:    device buffer of at least fd_decode_workspace_size(...) bytes,
  *               any contents (it needs no clearing: counters in it are
- *               tagged with a per-launch epoch), or NULL to use a
- *               library-owned per-device buffer.  One workspace must not be
+ *               tagged with a per-launch epoch that the kernel keeps in the
+ *               workspace), or NULL to use a library-owned per-device buffer
+ *               (allocated on first use: make one call before capturing a
+ *               CUDA graph, or pass a workspace).  One workspace must not be
  *               used by two calls that can run at the same time.
  * stream:       cudaStream_t (NULL = legacy default stream).
  * Returns FD_OK or an FD_ERR_* code; launches are asynchronous.
