@@ -45,19 +45,23 @@ namespace fd {
 
 namespace {
 
-// Stage / buffer geometry, by K/V element type.
+// Stage / buffer geometry, by K/V element type (and, for e4m3, query rows).
 //   16-bit K/V: a 128-token K or V tile is two 64-dim halves of 128 B rows
 //   (16 KB each, 128B-swizzled); the group's query rows ride in each stage;
 //   P is two 16-bit parts (hi = round(P), lo = round(P - hi)) side by side in
 //   the UMMA N dimension, so summing V.hi and V.lo keeps P's fp32 precision.
-//   e4m3 K/V: one 128 B row holds all 128 dims, a tile is 16 KB; the query
-//   rows arrive pre-split into three e4m3 parts (48 rows of 128 B) and P is
-//   split into three e4m3 parts the same way (see the softmax warps).
+//   e4m3 K/V: one 128 B row holds all 128 dims, a tile is 16 KB; each stage
+//   carries the query rows as three e4m3 parts (48 rows of 128 B, split by
+//   the K producer warp) and P is split into three e4m3 parts the same way
+//   (see the softmax warps).  Four stages up to 8 query rows, five at 16
+//   (more softmax work per tile wants a deeper ring; with less, a fifth
+//   stage only adds requests in flight to a saturated memory system:
+//   measured 3 % slower).
 // S^T tiles rotate through three TMEM buffers, P and O^T through two.  PV(i)
 // may overwrite O buffer i%2 once P(i) is written, since each softmax thread
 // loads O(i-2) before it writes P(i): the O buffers need no "empty" barrier.
-template <bool KV8> struct Geo {
-  static constexpr int kStages = KV8 ? 5 : 3;
+template <bool KV8, int NCOL = kMaxGroup> struct Geo {
+  static constexpr int kStages = KV8 ? (NCOL <= 8 ? 4 : 5) : 3;
   static constexpr int kHalfBytes = kTileTokens * 128;              // 128 rows x 128 B
   static constexpr int kOperandBytes = KV8 ? kHalfBytes : 2 * kHalfBytes;  // one K or V tile
   static constexpr int kParts = KV8 ? 3 : 2;                        // P (and Q) parts
@@ -425,7 +429,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
                         const __grid_constant__ CUtensorMap tm_v,
                         const __grid_constant__ CUtensorMap tm_k16,
                         const __grid_constant__ CUtensorMap tm_v16, const DecodeParams p) {
-  using G = Geo<KV8>;
+  using G = Geo<KV8, NCOL>;
   // 16-bit P.V uses N = 2*NL columns: NL hi parts then NL lo parts of P.
   // NCOL query rows are computed per (sequence, KV head); the 16-bit P
   // layout holds NL >= 8 columns per part (a UMMA needs N >= 16), the
@@ -1251,7 +1255,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
 
 template <typename T, typename OutT, int NCOL, bool MULTI, bool XCHG = false, bool KV8 = false>
 cudaError_t launch_typed(const TensorMaps& m, const DecodeParams& p, int grid, cudaStream_t stream) {
-  using G = Geo<KV8>;
+  using G = Geo<KV8, NCOL>;
   auto kern = decode_sm100_kernel<T, OutT, NCOL, MULTI, XCHG, KV8>;
   // The attribute is per device; setting it again is harmless.
   static unsigned long long configured = 0;
