@@ -1281,7 +1281,7 @@ cudaError_t launch_typed(const TensorMaps& m, const DecodeParams& p, int grid, c
   return cudaLaunchKernelEx(&cfg, kern, m.q, m.k, m.v, m.k16, m.v16, p);
 }
 
-// e4m3 K/V; T is the query type (its rows arrive pre-split into e4m3 parts).
+// e4m3 K/V; T is the query type (the kernel splits its rows into e4m3 parts).
 template <typename T, typename OutT>
 cudaError_t launch_ncol_kv8(const TensorMaps& m, const DecodeParams& p, int grid,
                             cudaStream_t stream) {
