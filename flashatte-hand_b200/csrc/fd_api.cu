@@ -27,6 +27,12 @@ constexpr int kMaxDevices = 64;
 constexpr unsigned long long kDefaultTimeoutNs = 1000000000ull;  // 1 s per in-kernel wait
 constexpr int kDefaultCostTile = 2;
 constexpr int kDefaultCostSeg = 12;
+// e4m3 caches: a tile carries half the bytes for the same fixed work, and a
+// pair also pays the in-kernel query split.  Swept on config 3's skewed
+// lengths (log-uniform 16 .. 32768): the 16-bit weights left CTAs with many
+// short sequences overloaded (295 us); these give 198 us.
+constexpr int kDefaultCostTile8 = 8;
+constexpr int kDefaultCostSeg8 = 48;
 
 thread_local int t_last_error = FD_OK;
 thread_local char t_last_msg[256] = "ok";
@@ -191,20 +197,23 @@ CUresult kv_maps(fd::TensorMaps& m, int dtype, const void* k, const void* v, int
 }
 
 // Split cost model (units: a full tile's K/V bytes = 8): fixed cost per
-// tile and per (sequence, KV head) pair.  FD_COST_TILE / FD_COST_SEG override.
+// tile and per (sequence, KV head) pair.  FD_COST_TILE / FD_COST_SEG override
+// them for 16-bit caches, FD_COST_TILE8 / FD_COST_SEG8 for e4m3 caches.
 int env_int(const char* name, int dflt, int lo, int hi) {
   const char* e = std::getenv(name);
   if (e == nullptr) return dflt;
   const long x = std::strtol(e, nullptr, 10);
   return (x >= lo && x <= hi) ? static_cast<int>(x) : dflt;
 }
-int cost_tile() {
+int cost_tile(bool kv8 = false) {
   static const int v = env_int("FD_COST_TILE", kDefaultCostTile, 0, 64);
-  return v;
+  static const int v8 = env_int("FD_COST_TILE8", kDefaultCostTile8, 0, 64);
+  return kv8 ? v8 : v;
 }
-int cost_seg() {
+int cost_seg(bool kv8 = false) {
   static const int v = env_int("FD_COST_SEG", kDefaultCostSeg, 1, 256);
-  return v;
+  static const int v8 = env_int("FD_COST_SEG8", kDefaultCostSeg8, 1, 256);
+  return kv8 ? v8 : v;
 }
 
 // Programmatic dependent launch of the decode kernel (FD_PDL=0 turns it off):
@@ -737,8 +746,8 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
     if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "K/V tensor map encode failed (%d)", (int)r);
   }
   const int64_t per_seq_cost =
-      cost_seg() + ((kv_max + fd::kTileTokens - 1) / fd::kTileTokens + 1) *
-                       (8 + static_cast<int64_t>(cost_tile()));
+      cost_seg(true) + ((kv_max + fd::kTileTokens - 1) / fd::kTileTokens + 1) *
+                       (8 + static_cast<int64_t>(cost_tile(true)));
   if (per_seq_cost > INT32_MAX) return set_error(FD_ERR_UNSUPPORTED, "sequence too long");
   int64_t per_launch = INT32_MAX / per_seq_cost;
   if (per_launch > fd::kMaxBatchPerLaunch) per_launch = fd::kMaxBatchPerLaunch;
@@ -769,8 +778,8 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
     p.part_o = reinterpret_cast<float*>(ws + wl.o_off);
     p.timeout_ns = timeout_ns();
     p.epoch_word = reinterpret_cast<uint32_t*>(ws + wl.epoch_off);
-    p.cost_tile = cost_tile();
-    p.cost_seg = cost_seg();
+    p.cost_tile = cost_tile(true);
+    p.cost_seg = cost_seg(true);
     p.xworld = 0;
     p.pdl = pdl_enabled() ? 1 : 0;
     p.len_add = len_add;
