@@ -247,18 +247,17 @@ def main():
         splitter = fdist.PeerSplitKVDecode(case.B, case.Hq, case.D, case.dtype, "cuda")
     fp8 = args.kv == "fp8"
     if fp8:
-        if splitter is not None:
-            raise SystemExit("--kv fp8 runs the single-GPU and batch-sharded modes only")
         del t
         torch.cuda.empty_cache()
-        t = cases.materialize_e4m3(case, "cuda", seed=rank)
+        # split-KV ranks share one query (seed 0), as above
+        t = cases.materialize_e4m3(case, "cuda", seed=0 if splitter is not None else rank)
         total_kv //= 2
     kv_kw = dict(k_scale=t["k_scale"], v_scale=t["v_scale"]) if fp8 else {}
     max_len = max(int(case.seqlens.max()), 1)
 
     def decode(q, seqlens, bt):
         if splitter is not None:
-            return splitter(q, t["k_cache"], t["v_cache"], seqlens, bt, case.softmax_scale)
+            return splitter(q, t["k_cache"], t["v_cache"], seqlens, bt, case.softmax_scale, **kv_kw)
         return flashdecode.flash_decode(q, t["k_cache"], t["v_cache"], seqlens, bt,
                                         softmax_scale=case.softmax_scale, return_softmax_lse=True,
                                         max_seqlen_k=max_len, **kv_kw)

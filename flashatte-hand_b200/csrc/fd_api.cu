@@ -482,6 +482,49 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
   return set_ok();
 }
 
+// One cross-GPU split-KV step (see fd_decode_paged_xgpu in the header):
+// this rank's exchange arguments for `step`, then `decode(xa, err)` (the
+// decode kernel in exchange mode, fp32 parts to every rank), then the merge
+// of all ranks' parts into out / lse on this rank.
+template <typename Decode>
+int xgpu_step(int64_t batch_size, int64_t seqlen_q, int64_t num_heads, int rank, int world,
+              void* const* xbufs, uint64_t step, void* out, int out_dtype, float* lse,
+              void* stream, Decode&& decode) {
+  if (xbufs == nullptr || out == nullptr) return set_error(FD_ERR_INVALID_ARG, "null pointer");
+  if (world < 1 || world > fd::kMaxExchangeRanks || rank < 0 || rank >= world)
+    return set_error(FD_ERR_INVALID_ARG, "rank %d / world %d", rank, world);
+  if (batch_size <= 0 || seqlen_q <= 0 || num_heads <= 0)
+    return set_error(FD_ERR_INVALID_ARG, "sizes must be positive");
+  for (int j = 0; j < world; ++j)
+    if (xbufs[j] == nullptr) return set_error(FD_ERR_INVALID_ARG, "exchange buffer %d is null", j);
+  const int64_t rows = batch_size * seqlen_q * num_heads;
+  const int64_t part = ((rows * (fd::kHeadDim + 1) + 63) / 64) * 64;
+  const int half = static_cast<int>(step & 1);
+  // Buffer: [flags half 0 | flags half 1 | parts half 0 | parts half 1],
+  // flags 256 B per half (one u32 per rank), parts world * `part` floats.
+  ExchangeArgs xa;
+  xa.world = world;
+  xa.lse_off = rows * fd::kHeadDim;
+  xa.epoch = static_cast<uint32_t>(step % 0x7FFFFFFFull) + 1u;
+  for (int j = 0; j < world; ++j) {
+    uint8_t* base = static_cast<uint8_t*>(xbufs[j]);
+    xa.flag[j] = reinterpret_cast<uint32_t*>(base + half * 256) + rank;
+    xa.part[j] = reinterpret_cast<float*>(base + 512) + (static_cast<int64_t>(half) * world + rank) * part;
+  }
+  int* err = nullptr;
+  const int st = decode(&xa, &err);
+  if (st != FD_OK) return st;
+  uint8_t* mine = static_cast<uint8_t*>(xbufs[rank]);
+  const float* parts = reinterpret_cast<const float*>(mine + 512) + static_cast<int64_t>(half) * world * part;
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(mine + half * 256);
+  const cudaError_t e = fd::launch_exchange_combine(
+      parts, part, rows * fd::kHeadDim, flags, world, xa.epoch, rows, static_cast<int>(seqlen_q),
+      static_cast<int>(num_heads), out, out_dtype, lse, err, timeout_ns(),
+      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "exchange combine: %s", cudaGetErrorString(e));
+  return set_ok();
+}
+
 }  // namespace
 
 extern "C" {
@@ -554,45 +597,17 @@ int fd_decode_paged_xgpu(const void* q, const void* k_cache, const void* v_cache
                          float softmax_scale, int causal, int64_t max_seqlen_k, int rank,
                          int world, void* const* xbufs, uint64_t step, void* out, float* lse,
                          void* workspace, size_t workspace_bytes, void* stream) {
-  if (xbufs == nullptr || out == nullptr) return set_error(FD_ERR_INVALID_ARG, "null pointer");
-  if (world < 1 || world > fd::kMaxExchangeRanks || rank < 0 || rank >= world)
-    return set_error(FD_ERR_INVALID_ARG, "rank %d / world %d", rank, world);
-  if (batch_size <= 0 || seqlen_q <= 0 || num_heads <= 0)
-    return set_error(FD_ERR_INVALID_ARG, "sizes must be positive");
   if (out_dtype != dtype && out_dtype != FD_DTYPE_FP32)
     return set_error(FD_ERR_INVALID_ARG, "out_dtype must equal dtype or be fp32");
-  for (int j = 0; j < world; ++j)
-    if (xbufs[j] == nullptr) return set_error(FD_ERR_INVALID_ARG, "exchange buffer %d is null", j);
-  const int64_t rows = batch_size * seqlen_q * num_heads;
-  const int64_t part = ((rows * (fd::kHeadDim + 1) + 63) / 64) * 64;
-  const int half = static_cast<int>(step & 1);
-  // Buffer: [flags half 0 | flags half 1 | parts half 0 | parts half 1],
-  // flags 256 B per half (one u32 per rank), parts world * `part` floats.
-  ExchangeArgs xa;
-  xa.world = world;
-  xa.lse_off = rows * fd::kHeadDim;
-  xa.epoch = static_cast<uint32_t>(step % 0x7FFFFFFFull) + 1u;
-  for (int j = 0; j < world; ++j) {
-    uint8_t* base = static_cast<uint8_t*>(xbufs[j]);
-    xa.flag[j] = reinterpret_cast<uint32_t*>(base + half * 256) + rank;
-    xa.part[j] = reinterpret_cast<float*>(base + 512) + (static_cast<int64_t>(half) * world + rank) * part;
-  }
-  int* err = nullptr;
-  const int st = decode_impl(q, k_cache, v_cache, nullptr, nullptr, cache_seqlens, block_table,
-                             block_table_stride, batch_size, seqlen_q, num_heads, num_heads_k,
-                             headdim, page_block_size, num_blocks, dtype, FD_DTYPE_FP32,
-                             softmax_scale, causal, max_seqlen_k, 0, workspace, workspace_bytes,
-                             stream, &xa, &err);
-  if (st != FD_OK) return st;
-  uint8_t* mine = static_cast<uint8_t*>(xbufs[rank]);
-  const float* parts = reinterpret_cast<const float*>(mine + 512) + static_cast<int64_t>(half) * world * part;
-  const uint32_t* flags = reinterpret_cast<const uint32_t*>(mine + half * 256);
-  const cudaError_t e = fd::launch_exchange_combine(
-      parts, part, rows * fd::kHeadDim, flags, world, xa.epoch, rows, static_cast<int>(seqlen_q),
-      static_cast<int>(num_heads), out, out_dtype, lse, err, timeout_ns(),
-      static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "exchange combine: %s", cudaGetErrorString(e));
-  return set_ok();
+  return xgpu_step(batch_size, seqlen_q, num_heads, rank, world, xbufs, step, out, out_dtype, lse,
+                   stream, [&](const ExchangeArgs* xa, int** err) {
+                     return decode_impl(q, k_cache, v_cache, nullptr, nullptr, cache_seqlens,
+                                        block_table, block_table_stride, batch_size, seqlen_q,
+                                        num_heads, num_heads_k, headdim, page_block_size,
+                                        num_blocks, dtype, FD_DTYPE_FP32, softmax_scale, causal,
+                                        max_seqlen_k, 0, workspace, workspace_bytes, stream, xa,
+                                        err);
+                   });
 }
 
 int fd_append_kv_paged(const void* k_new, const void* v_new, void* k_cache, void* v_cache,
@@ -713,10 +728,14 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
                            int64_t num_heads, int64_t num_heads_k, int64_t page_block_size,
                            int64_t num_blocks, int q_dtype, int out_dtype, float softmax_scale,
                            int causal, int64_t max_seqlen_k, int len_add, void* workspace,
-                           size_t workspace_bytes, void* stream) {
+                           size_t workspace_bytes, void* stream,
+                           const ExchangeArgs* xa = nullptr, int** err_word = nullptr) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices)
     return set_error(FD_ERR_CUDA, "no current CUDA device");
+  if (xa != nullptr && batch_size > fd::kMaxBatchPerLaunch)
+    return set_error(FD_ERR_UNSUPPORTED, "cross-GPU exchange takes at most %d sequences",
+                     fd::kMaxBatchPerLaunch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int group = static_cast<int>(num_heads / num_heads_k);
   const int64_t qrows = seqlen_q * group;
@@ -781,11 +800,24 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
     p.cost_tile = cost_tile(true);
     p.cost_seg = cost_seg(true);
     p.xworld = 0;
-    p.pdl = pdl_enabled() ? 1 : 0;
+    p.pdl = (xa == nullptr && pdl_enabled()) ? 1 : 0;
     p.len_add = len_add;
     p.k_scale = k_scale;
     p.v_scale = v_scale;
     p.q = qb;
+    if (xa != nullptr) {
+      p.xworld = xa->world;
+      for (int j = 0; j < fd::kMaxExchangeRanks; ++j) {
+        p.xpart[j] = j < xa->world ? xa->part[j] : nullptr;
+        p.xflag[j] = j < xa->world ? xa->flag[j] : nullptr;
+      }
+      p.xlse_off = xa->lse_off;
+      p.xepoch = xa->epoch;
+      p.xdone = reinterpret_cast<uint32_t*>(ws + wl.done_off);
+      const cudaError_t ez = cudaMemsetAsync(p.xdone, 0, sizeof(uint32_t), st);
+      if (ez != cudaSuccess) return set_error(FD_ERR_CUDA, "clear done counter: %s", cudaGetErrorString(ez));
+    }
+    if (err_word != nullptr) *err_word = p.err;
     const int64_t work_bound = nb * num_heads_k * tiles_bound;
     const int grid = static_cast<int>(work_bound < sms ? work_bound : sms);
     const cudaError_t e = fd::launch_decode_sm100_kv8(maps, p, q_dtype, out_dtype == FD_DTYPE_FP32, grid, st);
@@ -805,6 +837,31 @@ size_t fd_decode_workspace_size_fp8(int64_t batch_size, int64_t seqlen_q, int64_
   if (sms <= 0) return 0;
   const int64_t nb = batch_size < fd::kMaxBatchPerLaunch ? batch_size : fd::kMaxBatchPerLaunch;
   return fd::workspace_layout(nb, num_heads_k, seqlen_q * (num_heads / num_heads_k), sms).total;
+}
+
+int fd_decode_paged_fp8_xgpu(const void* q, const void* k_cache, const void* v_cache,
+                             const float* k_scale, const float* v_scale,
+                             const int32_t* cache_seqlens, const int32_t* block_table,
+                             int64_t block_table_stride, int64_t batch_size, int64_t seqlen_q,
+                             int64_t num_heads, int64_t num_heads_k, int64_t headdim,
+                             int64_t page_block_size, int64_t num_blocks, int q_dtype,
+                             int out_dtype, float softmax_scale, int causal, int64_t max_seqlen_k,
+                             int rank, int world, void* const* xbufs, uint64_t step, void* out,
+                             float* lse, void* workspace, size_t workspace_bytes, void* stream) {
+  const int st = check_kv8_args(q, k_cache, v_cache, k_scale, v_scale, out, cache_seqlens,
+                                block_table, block_table_stride, batch_size, seqlen_q, num_heads,
+                                num_heads_k, headdim, page_block_size, num_blocks, q_dtype,
+                                out_dtype, softmax_scale);
+  if (st != FD_OK) return st;
+  return xgpu_step(batch_size, seqlen_q, num_heads, rank, world, xbufs, step, out, out_dtype, lse,
+                   stream, [&](const ExchangeArgs* xa, int** err) {
+                     return decode_kv8_impl(q, k_cache, v_cache, k_scale, v_scale, nullptr, nullptr,
+                                            cache_seqlens, block_table, block_table_stride,
+                                            batch_size, seqlen_q, num_heads, num_heads_k,
+                                            page_block_size, num_blocks, q_dtype, FD_DTYPE_FP32,
+                                            softmax_scale, causal, max_seqlen_k, 0, workspace,
+                                            workspace_bytes, stream, xa, err);
+                   });
 }
 
 int fd_append_kv_paged_fp8(const void* k_new, const void* v_new, void* k_cache, void* v_cache,

@@ -1286,6 +1286,15 @@ template <typename T, typename OutT>
 cudaError_t launch_ncol_kv8(const TensorMaps& m, const DecodeParams& p, int grid,
                             cudaStream_t stream) {
   const bool multi = p.seqlen_q > 1 || p.causal;
+  if constexpr (std::is_same<OutT, float>::value) {
+    if (p.xworld > 0) {  // cross-GPU exchange: fp32 parts to every rank
+      if (p.qrows <= 8)
+        return multi ? launch_typed<T, float, 8, true, true, true>(m, p, grid, stream)
+                     : launch_typed<T, float, 8, false, true, true>(m, p, grid, stream);
+      return multi ? launch_typed<T, float, 16, true, true, true>(m, p, grid, stream)
+                   : launch_typed<T, float, 16, false, true, true>(m, p, grid, stream);
+    }
+  }
   if (p.qrows <= 4)
     return multi ? launch_typed<T, OutT, 4, true, false, true>(m, p, grid, stream)
                  : launch_typed<T, OutT, 4, false, false, true>(m, p, grid, stream);

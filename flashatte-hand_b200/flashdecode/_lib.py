@@ -43,6 +43,9 @@ SIGNATURES: dict[str, tuple] = {
     "fd_decode_paged_xgpu": (_i32, [_vp, _vp, _vp, _vp, _vp] + [_i64] * 8
                              + [_i32, _i32, _f32, _i32, _i64, _i32, _i32, _c.POINTER(_vp),
                                 _c.c_uint64, _vp, _vp, _vp, _sz, _vp]),
+    "fd_decode_paged_fp8_xgpu": (_i32, [_vp] * 7 + [_i64] * 8
+                                 + [_i32, _i32, _f32, _i32, _i64, _i32, _i32, _c.POINTER(_vp),
+                                    _c.c_uint64, _vp, _vp, _vp, _sz, _vp]),
     "fd_last_error": (_i32, []),
     "fd_error_string": (_c.c_char_p, [_i32]),
     "fd_last_error_message": (_c.c_char_p, []),

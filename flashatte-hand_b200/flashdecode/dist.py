@@ -195,7 +195,9 @@ class PeerSplitKVDecode:
         tdist.barrier(group=group)
 
     def __call__(self, q, k_local, v_local, seqlens_local, bt_local, softmax_scale: float,
-                 causal: bool = False, out=None, lse=None):
+                 causal: bool = False, out=None, lse=None, k_scale=None, v_scale=None):
+        """One step.  e4m3 caches (torch.float8_e4m3fn) take fp32 per-KV-head
+        k_scale / v_scale [Hkv], as flashdecode.flash_decode does."""
         B, sq, Hq, D = q.shape
         if out is None:
             out = torch.empty((B, sq, Hq, D), dtype=self.out_dtype, device=q.device)
@@ -205,12 +207,23 @@ class PeerSplitKVDecode:
         st = torch.cuda.current_stream(q.device)
         nb, page, Hkv, _ = k_local.shape
         with torch.cuda.device(q.device):
-            status = self.lib.fd_decode_paged_xgpu(
-                q.data_ptr(), k_local.data_ptr(), v_local.data_ptr(), seqlens_local.data_ptr(),
-                bt_local.data_ptr(), bt_local.shape[1], B, sq, Hq, Hkv, D, page, nb, _DT[q.dtype],
-                _DT[self.out_dtype], float(softmax_scale), 1 if causal else 0, 0, self.rank,
-                self.world, self.xbufs, self.step, out.data_ptr(), lse.data_ptr(), None, 0,
-                st.cuda_stream)
+            if k_local.dtype == torch.float8_e4m3fn:
+                if k_scale is None or v_scale is None:
+                    raise ValueError("e4m3 caches need k_scale and v_scale")
+                status = self.lib.fd_decode_paged_fp8_xgpu(
+                    q.data_ptr(), k_local.data_ptr(), v_local.data_ptr(), k_scale.data_ptr(),
+                    v_scale.data_ptr(), seqlens_local.data_ptr(), bt_local.data_ptr(),
+                    bt_local.shape[1], B, sq, Hq, Hkv, D, page, nb, _DT[q.dtype],
+                    _DT[self.out_dtype], float(softmax_scale), 1 if causal else 0, 0, self.rank,
+                    self.world, self.xbufs, self.step, out.data_ptr(), lse.data_ptr(), None, 0,
+                    st.cuda_stream)
+            else:
+                status = self.lib.fd_decode_paged_xgpu(
+                    q.data_ptr(), k_local.data_ptr(), v_local.data_ptr(), seqlens_local.data_ptr(),
+                    bt_local.data_ptr(), bt_local.shape[1], B, sq, Hq, Hkv, D, page, nb, _DT[q.dtype],
+                    _DT[self.out_dtype], float(softmax_scale), 1 if causal else 0, 0, self.rank,
+                    self.world, self.xbufs, self.step, out.data_ptr(), lse.data_ptr(), None, 0,
+                    st.cuda_stream)
         check(status)
         self.step += 1
         return out, lse

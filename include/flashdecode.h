@@ -289,6 +289,24 @@ int fd_decode_paged_xgpu(const void* q, const void* k_cache, const void* v_cache
                          int world, void* const* xbufs, uint64_t step, void* out, float* lse,
                          void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * fd_decode_paged_fp8_xgpu - fd_decode_paged_xgpu over an e4m3 KV cache:
+ * the same step, exchange buffers and merge, with k_cache / v_cache and
+ * k_scale / v_scale as in fd_decode_paged_fp8 (q of type q_dtype, bf16 or
+ * fp16; no cache append).  Same limits as fd_decode_paged_fp8 and
+ * batch_size <= 512.
+ * Replaces: nothing in the reference (no FP8 cache, no multi-GPU code).
+ */
+int fd_decode_paged_fp8_xgpu(const void* q, const void* k_cache, const void* v_cache,
+                             const float* k_scale, const float* v_scale,
+                             const int32_t* cache_seqlens, const int32_t* block_table,
+                             int64_t block_table_stride, int64_t batch_size, int64_t seqlen_q,
+                             int64_t num_heads, int64_t num_heads_k, int64_t headdim,
+                             int64_t page_block_size, int64_t num_blocks, int q_dtype,
+                             int out_dtype, float softmax_scale, int causal, int64_t max_seqlen_k,
+                             int rank, int world, void* const* xbufs, uint64_t step, void* out,
+                             float* lse, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Status of the last call made on this host thread, and its message. */
 int fd_last_error(void);
 const char* fd_error_string(int code);

@@ -42,17 +42,20 @@ def _worker(rank, port, kind, q):
                                 device_id=torch.device("cuda", rank))
         glob = cases.custom_case("mg", torch.bfloat16, [20000, 3, 7777, 0, 40000], 32, 8,
                                  page=256, seed=5)
-        t = cases.materialize(glob, "cuda", seed=5)  # identical on every rank
+        fp8 = kind == "peer_fp8"
+        # identical on every rank
+        t = (cases.materialize_e4m3 if fp8 else cases.materialize)(glob, "cuda", seed=5)
+        kw = dict(k_scale=t["k_scale"], v_scale=t["v_scale"]) if fp8 else {}
         ref_o, ref_l = flashdecode.flash_decode(t["q"], t["k_cache"], t["v_cache"], t["cache_seqlens"],
-                                                t["block_table"], return_softmax_lse=True)
-        if kind == "peer":
+                                                t["block_table"], return_softmax_lse=True, **kw)
+        if kind in ("peer", "peer_fp8"):
             local, page_map = fdist.kv_split_case(glob, rank, WORLD)
             pm = page_map.to("cuda")
             k, v = t["k_cache"][pm].contiguous(), t["v_cache"][pm].contiguous()
             step = fdist.PeerSplitKVDecode(glob.B, glob.Hq, glob.D, torch.bfloat16, "cuda")
             for _ in range(5):  # both buffer halves, several epochs
                 out, lse = step(t["q"], k, v, local.seqlens.cuda(), local.block_table.cuda(),
-                                glob.softmax_scale)
+                                glob.softmax_scale, **kw)
             torch.cuda.synchronize()
             assert flashdecode.device_status() == 0
             err = (out.float() - ref_o.float()).abs()
@@ -136,6 +139,11 @@ def test_split_kv_across_two_gpus():
 
 def test_split_kv_over_peer_memory_two_gpus():
     _run("peer")
+
+
+def test_split_kv_over_peer_memory_two_gpus_e4m3_cache():
+    """The same exchange with an e4m3 cache, against the single-GPU e4m3 result."""
+    _run("peer_fp8")
 
 
 def test_batch_shard_across_two_gpus():
