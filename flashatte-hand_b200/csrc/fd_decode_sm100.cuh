@@ -871,16 +871,34 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       tc_fence_after();
       if constexpr (KV8) {
         // three parts of P, 16 columns apart: O = O0 + O1 / 16 + O2 / 256
-        uint32_t r0[NCOL], r1[NCOL], r2[NCOL];
-        tmem_ld_cols<NCOL>(lane_addr + G::col_o(pb), r0);
-        tmem_ld_cols<NCOL>(lane_addr + G::col_o(pb) + kMaxGroup, r1);
-        tmem_ld_cols<NCOL>(lane_addr + G::col_o(pb) + 2 * kMaxGroup, r2);
-        tmem_wait_ld();
-        tc_fence_before();  // orders this load before the next P arrival (frees the O buffer)
+        if constexpr (NCOL == kMaxGroup) {
+          // 16 rows: one part at a time (same sums, 32 fewer live registers)
+          uint32_t r0[NCOL];
+          tmem_ld_cols<NCOL>(lane_addr + G::col_o(pb), r0);
+          tmem_wait_ld();
 #pragma unroll
-        for (int h = 0; h < NCOL; ++h)
-          ov[h] = fmaf(__uint_as_float(r2[h]), 1.f / 256.f,
-                       fmaf(__uint_as_float(r1[h]), 1.f / 16.f, __uint_as_float(r0[h])));
+          for (int h = 0; h < NCOL; ++h) ov[h] = __uint_as_float(r0[h]);
+          tmem_ld_cols<NCOL>(lane_addr + G::col_o(pb) + kMaxGroup, r0);
+          tmem_wait_ld();
+#pragma unroll
+          for (int h = 0; h < NCOL; ++h) ov[h] = fmaf(__uint_as_float(r0[h]), 1.f / 16.f, ov[h]);
+          tmem_ld_cols<NCOL>(lane_addr + G::col_o(pb) + 2 * kMaxGroup, r0);
+          tmem_wait_ld();
+          tc_fence_before();  // orders these loads before the next P arrival (frees the O buffer)
+#pragma unroll
+          for (int h = 0; h < NCOL; ++h) ov[h] = fmaf(__uint_as_float(r0[h]), 1.f / 256.f, ov[h]);
+        } else {
+          uint32_t r0[NCOL], r1[NCOL], r2[NCOL];
+          tmem_ld_cols<NCOL>(lane_addr + G::col_o(pb), r0);
+          tmem_ld_cols<NCOL>(lane_addr + G::col_o(pb) + kMaxGroup, r1);
+          tmem_ld_cols<NCOL>(lane_addr + G::col_o(pb) + 2 * kMaxGroup, r2);
+          tmem_wait_ld();
+          tc_fence_before();  // orders this load before the next P arrival (frees the O buffer)
+#pragma unroll
+          for (int h = 0; h < NCOL; ++h)
+            ov[h] = fmaf(__uint_as_float(r2[h]), 1.f / 256.f,
+                         fmaf(__uint_as_float(r1[h]), 1.f / 16.f, __uint_as_float(r0[h])));
+        }
       } else {
         uint32_t r[kPvN];
         if constexpr (NL == 8) tmem_ld_x16(lane_addr + G::col_o(pb), r); else tmem_ld_x32(lane_addr + G::col_o(pb), r);
@@ -1096,15 +1114,31 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         const uint32_t cs = G::col_s(static_cast<int>(it % G::kSBufs));
         if constexpr (KV8) {
           // three parts of the query, 16 columns apart: S = S0 + S1 / 16 + S2 / 256
-          uint32_t r1[NCOL], r2[NCOL];
-          tmem_ld_cols<NCOL>(lane_addr + cs, r);
-          tmem_ld_cols<NCOL>(lane_addr + cs + kMaxGroup, r1);
-          tmem_ld_cols<NCOL>(lane_addr + cs + 2 * kMaxGroup, r2);
-          tmem_wait_ld();
+          if constexpr (NCOL == kMaxGroup) {
+            // 16 rows: one part at a time (same sums, 32 fewer live registers)
+            tmem_ld_cols<NCOL>(lane_addr + cs, r);
+            tmem_wait_ld();
 #pragma unroll
-          for (int h = 0; h < NCOL; ++h)
-            s8[h] = fmaf(__uint_as_float(r2[h]), 1.f / 256.f,
-                         fmaf(__uint_as_float(r1[h]), 1.f / 16.f, __uint_as_float(r[h])));
+            for (int h = 0; h < NCOL; ++h) s8[h] = __uint_as_float(r[h]);
+            tmem_ld_cols<NCOL>(lane_addr + cs + kMaxGroup, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int h = 0; h < NCOL; ++h) s8[h] = fmaf(__uint_as_float(r[h]), 1.f / 16.f, s8[h]);
+            tmem_ld_cols<NCOL>(lane_addr + cs + 2 * kMaxGroup, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int h = 0; h < NCOL; ++h) s8[h] = fmaf(__uint_as_float(r[h]), 1.f / 256.f, s8[h]);
+          } else {
+            uint32_t r1[NCOL], r2[NCOL];
+            tmem_ld_cols<NCOL>(lane_addr + cs, r);
+            tmem_ld_cols<NCOL>(lane_addr + cs + kMaxGroup, r1);
+            tmem_ld_cols<NCOL>(lane_addr + cs + 2 * kMaxGroup, r2);
+            tmem_wait_ld();
+#pragma unroll
+            for (int h = 0; h < NCOL; ++h)
+              s8[h] = fmaf(__uint_as_float(r2[h]), 1.f / 256.f,
+                           fmaf(__uint_as_float(r1[h]), 1.f / 16.f, __uint_as_float(r[h])));
+          }
         } else {
           tmem_ld_cols<NCOL>(lane_addr + cs, r);
           tmem_wait_ld();
