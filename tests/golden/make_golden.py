@@ -6,9 +6,9 @@ flash_attn.flash_attn_interface.flash_attn_with_kvcache
 flash_attn 2.6.3, here 2.8.3).  That library is CUDA-only, so this script
 runs on a GPU box:
 
-    python tests/golden/make_golden.py --out gpurun_out/golden
+    python tests/golden/make_golden.py --out golden_out
 
-and writes ``fa_golden.json`` (case specs, library versions) and
+(then copy the files into tests/golden/) and writes ``fa_golden.json`` (case specs, library versions) and
 ``fa_golden.npz`` (out, lse per case).  With ``--append`` it writes
 ``fa_golden_append.*`` instead: cases that pass new keys/values (k, v) so
 flash_attn first appends them to the paged cache, with 1-4 query tokens and
