@@ -94,7 +94,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 
 // 4-D tiled loads into this CTA's shared memory, completing on `bar`
 // with a byte count.  `policy` is an L2 cache-policy descriptor made by
-// createpolicy.  Never used with .multicast::cluster.
+// createpolicy.  Plain loads only: no cluster-multicast form.
 __device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* bar, void* dst,
                                             int c0, int c1, int c2, int c3, uint64_t policy) {
   asm volatile(
@@ -107,7 +107,7 @@ __device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* ba
 
 // Untiled bulk copy of `bytes` (a multiple of 16; both addresses 16-byte
 // aligned) from global memory into this CTA's shared memory, completing on
-// `bar` with a byte count.  Never used with .multicast::cluster.
+// `bar` with a byte count.  Plain copy only: no cluster-multicast form.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
