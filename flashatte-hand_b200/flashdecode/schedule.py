@@ -23,6 +23,10 @@ MAX_BATCH_PER_LAUNCH = 512
 FULL_TILE = 8
 DEFAULT_TILE_FIXED = 2
 DEFAULT_SEG = 12
+# e4m3 caches (half the bytes per tile for the same fixed work, plus the
+# in-kernel query split per pair): the kernel's defaults for that path
+E4M3_TILE_FIXED = 8
+E4M3_SEG = 48
 
 
 @dataclass(frozen=True)

@@ -79,8 +79,11 @@ def test_lpt_partition_balances_skew(world):
     ([300, 7], 8, 148), ([1, 127, 128, 129, 300, 0, 1000, 2049], 4, 148),
     ([1, 127, 128, 129, 300, 0, 1000, 2049], 1, 148),
 ])
-def test_schedule_covers_every_tile_once(seqlens, hkv, grid):
-    segs = schedule.segments(seqlens, hkv, grid)
+@pytest.mark.parametrize("weights", ["16-bit", "e4m3"])
+def test_schedule_covers_every_tile_once(seqlens, hkv, grid, weights):
+    kw = (dict(tile_fixed=schedule.E4M3_TILE_FIXED, seg=schedule.E4M3_SEG) if weights == "e4m3"
+          else {})
+    segs = schedule.segments(seqlens, hkv, grid, **kw)
     seen = {}
     for s in segs:
         for t in range(s.tile0, s.tile0 + s.ntiles):
@@ -156,3 +159,14 @@ def test_head_shard_slices_heads_and_decodes_the_same_rows():
     assert covered == list(range(c.Hkv))
     with pytest.raises(ValueError):
         fdist.head_range(6, 0, 4)
+
+
+def test_cost_defaults_match_the_host_library():
+    """The mirror's cost weights are the ones fd_api.cu launches with."""
+    import re
+    from pathlib import Path
+    src = (Path(__file__).resolve().parent.parent / "flashatte-hand_b200" / "csrc" / "fd_api.cu").read_text()
+    got = {m.group(1): int(m.group(2))
+           for m in re.finditer(r"constexpr int (kDefaultCost\w+) = (\d+);", src)}
+    assert got == {"kDefaultCostTile": schedule.DEFAULT_TILE_FIXED, "kDefaultCostSeg": schedule.DEFAULT_SEG,
+                   "kDefaultCostTile8": schedule.E4M3_TILE_FIXED, "kDefaultCostSeg8": schedule.E4M3_SEG}
