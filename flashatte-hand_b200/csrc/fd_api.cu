@@ -6,7 +6,11 @@
 // fixed split table chosen from (batch, max length) and a grow-only static
 // workspace shared by every device and stream, the split is decided on the
 // device from cache_seqlens (stream-K ranges, see fd_decode_sm100.cu) and the
-// workspace is either the caller's or a per-device buffer.
+// workspace is either the caller's or a library-owned buffer per (device,
+// stream), so calls on different streams never share split scratch.  Errors
+// a kernel meets (a bounded wait that ran out, a page id outside the pool)
+// go to one status word per device inside this library, read and cleared by
+// fd_device_status whichever workspace the call used.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -17,6 +21,8 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <thread>
+#include <vector>
 
 #include "../../include/flashdecode.h"
 #include "fd_kernels.h"
@@ -73,11 +79,28 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// Status word of each device: the first error a kernel of this library met
+// since fd_device_status last read it (kStatusTimeout, kStatusBadPage).
+__device__ int g_device_status;
+
+// Library-owned workspace of one stream (streams passing workspace = NULL).
+// cudaStreamPerThread names a different stream in every host thread, so its
+// workspaces are also keyed by thread.
+struct StreamWorkspace {
+  cudaStream_t stream;
+  std::thread::id thread;
+  void* ptr;
+  size_t bytes;
+};
+
 struct DeviceState {
   std::mutex mu;
   int num_sms = 0;
-  void* ws = nullptr;
-  size_t ws_bytes = 0;
+  std::vector<StreamWorkspace> ws;       // the current workspace of each stream
+  std::vector<StreamWorkspace> retired;  // outgrown ones (graphs may still use them)
+  cudaStream_t zero_stream = nullptr;    // non-blocking: clears new workspaces
+  std::once_flag status_once;
+  int* status = nullptr;               // device address of g_device_status
 };
 DeviceState g_dev[kMaxDevices];
 
@@ -92,25 +115,61 @@ int device_sms(int dev) {
   return s.num_sms;
 }
 
-// Library-owned workspace of `dev`: grow-only, zero-filled when (re)allocated.
-void* internal_workspace(int dev, size_t bytes, cudaStream_t stream) {
+// Device address of the status word on `dev` (the current device): the
+// symbol's name is only a host-side stand-in, so it is looked up once per
+// device while that device is current.
+int* status_word(int dev) {
+  DeviceState& s = g_dev[dev];
+  std::call_once(s.status_once, [&s] {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_status) == cudaSuccess) s.status = static_cast<int*>(p);
+  });
+  return s.status;
+}
+
+// Library-owned workspace of (`dev`, `stream`): grow-only, zero-filled when
+// allocated, kept until the process exits.  A workspace that a larger call
+// outgrows is retired rather than freed, since a CUDA graph captured on the
+// stream may still use it.  A stream that is being captured gets its
+// workspace too: the allocation and the clearing are made under the relaxed
+// capture mode on an internal stream that is not captured, so nothing of
+// them enters the graph.
+void* internal_workspace(int dev, size_t bytes, cudaStream_t stream, const char** why) {
   DeviceState& s = g_dev[dev];
   std::lock_guard<std::mutex> lk(s.mu);
-  if (s.ws_bytes >= bytes) return s.ws;
-  if (s.ws != nullptr) {
-    cudaStreamSynchronize(stream);
-    cudaFree(s.ws);
-    s.ws = nullptr;
-    s.ws_bytes = 0;
-  }
-  void* p = nullptr;
-  if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
-  if (cudaMemset(p, 0, bytes) != cudaSuccess) {
-    cudaFree(p);
+  const std::thread::id tid =
+      stream == cudaStreamPerThread ? std::this_thread::get_id() : std::thread::id();
+  StreamWorkspace* e = nullptr;
+  for (StreamWorkspace& w : s.ws)
+    if (w.stream == stream && w.thread == tid) e = &w;
+  if (e != nullptr && e->bytes >= bytes) return e->ptr;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (stream != nullptr && cudaStreamIsCapturing(stream, &cs) != cudaSuccess) {
+    *why = "cannot query the stream's capture status";
     return nullptr;
   }
-  s.ws = p;
-  s.ws_bytes = bytes;
+  const bool capturing = cs != cudaStreamCaptureStatusNone;
+  cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+  if (capturing) cudaThreadExchangeStreamCaptureMode(&mode);
+  void* p = nullptr;
+  cudaError_t err = cudaSuccess;
+  if (s.zero_stream == nullptr) err = cudaStreamCreateWithFlags(&s.zero_stream, cudaStreamNonBlocking);
+  if (err == cudaSuccess) err = cudaMalloc(&p, bytes);
+  if (err == cudaSuccess) err = cudaMemsetAsync(p, 0, bytes, s.zero_stream);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(s.zero_stream);
+  if (capturing) cudaThreadExchangeStreamCaptureMode(&mode);
+  if (err != cudaSuccess) {
+    if (p != nullptr) cudaFree(p);
+    *why = "cannot allocate or clear the workspace";
+    return nullptr;
+  }
+  if (e != nullptr) {
+    s.retired.push_back(*e);
+    e->ptr = p;
+    e->bytes = bytes;
+  } else {
+    s.ws.push_back(StreamWorkspace{stream, tid, p, bytes});
+  }
   return p;
 }
 
@@ -118,11 +177,23 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int esize(int dtype) { return dtype == FD_DTYPE_FP32 ? 4 : 2; }
 
+// Tuning knobs (FD_TMA_CHUNK, FD_COST_TILE / FD_COST_SEG and their e4m3
+// twins, FD_PDL, FD_WAIT_TIMEOUT_NS) are read from the environment only when
+// FD_DEBUG_KNOBS=1: without that switch a caller's environment cannot change
+// the schedule or the timeouts of the operator.
+const char* knob(const char* name) {
+  static const bool enabled = [] {
+    const char* e = std::getenv("FD_DEBUG_KNOBS");
+    return e != nullptr && std::strcmp(e, "1") == 0;
+  }();
+  return enabled ? std::getenv(name) : nullptr;
+}
+
 // Tokens per TMA box for full tiles: the largest of 128/64/32/16 dividing the
-// page (a box never crosses a page).  FD_TMA_CHUNK lowers it (tuning aid).
+// page (a box never crosses a page).  FD_TMA_CHUNK lowers it (tuning knob).
 int pick_chunk(int64_t page) {
   static const int cap = [] {
-    const char* e = std::getenv("FD_TMA_CHUNK");
+    const char* e = knob("FD_TMA_CHUNK");
     const int v = e != nullptr ? std::atoi(e) : 128;
     return (v == 16 || v == 32 || v == 64) ? v : 128;
   }();
@@ -200,7 +271,7 @@ CUresult kv_maps(fd::TensorMaps& m, int dtype, const void* k, const void* v, int
 // tile and per (sequence, KV head) pair.  FD_COST_TILE / FD_COST_SEG override
 // them for 16-bit caches, FD_COST_TILE8 / FD_COST_SEG8 for e4m3 caches.
 int env_int(const char* name, int dflt, int lo, int hi) {
-  const char* e = std::getenv(name);
+  const char* e = knob(name);
   if (e == nullptr) return dflt;
   const long x = std::strtol(e, nullptr, 10);
   return (x >= lo && x <= hi) ? static_cast<int>(x) : dflt;
@@ -226,7 +297,7 @@ bool pdl_enabled() {
 
 unsigned long long timeout_ns() {
   static unsigned long long v = [] {
-    const char* e = std::getenv("FD_WAIT_TIMEOUT_NS");
+    const char* e = knob("FD_WAIT_TIMEOUT_NS");
     if (e != nullptr) {
       const unsigned long long x = std::strtoull(e, nullptr, 10);
       if (x > 0) return x;
@@ -239,6 +310,18 @@ unsigned long long timeout_ns() {
 }  // namespace
 
 namespace fd {
+int* device_status_word() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  return status_word(dev);
+}
+
+bool uses_tensor_core_path(const void* q, const void* k_cache, const void* v_cache,
+                           int64_t headdim, int64_t qrows, int64_t page_block_size) {
+  return headdim == kHeadDim && qrows <= kMaxGroup && pick_chunk(page_block_size) > 0 &&
+         aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && encode_fn() != nullptr;
+}
+
 int report_error(int code, const char* fmt, ...) {
   t_last_error = code;
   va_list ap;
@@ -265,6 +348,7 @@ const char* fd_error_string(int code) {
     case FD_ERR_WORKSPACE: return "workspace missing or too small";
     case FD_ERR_CUDA: return "CUDA error";
     case FD_ERR_DEVICE_TIMEOUT: return "in-kernel wait timed out";
+    case FD_ERR_BAD_PAGE: return "page id outside the KV pool";
     default: return "unknown error";
   }
 }
@@ -337,8 +421,10 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
     return set_error(FD_ERR_UNSUPPORTED, "size exceeds 32-bit index range");
 
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices)
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return set_error(FD_ERR_CUDA, "no current CUDA device");
+  int* status = status_word(dev);
+  if (status == nullptr) return set_error(FD_ERR_CUDA, "cannot find the device status word");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int group = static_cast<int>(num_heads / num_heads_k);
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
@@ -346,9 +432,8 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
   const int chunk = pick_chunk(page_block_size);
   const int64_t qrows = seqlen_q * group;
 
-  const bool tensor_core_path = headdim == fd::kHeadDim && qrows <= fd::kMaxGroup && chunk > 0 &&
-                                aligned16(q) && aligned16(k_cache) && aligned16(v_cache) &&
-                                encode_fn() != nullptr;
+  const bool tensor_core_path =
+      fd::uses_tensor_core_path(q, k_cache, v_cache, headdim, qrows, page_block_size);
   if (xa != nullptr && (!tensor_core_path || batch_size > fd::kMaxBatchPerLaunch))
     return set_error(FD_ERR_UNSUPPORTED,
                      "cross-GPU exchange needs the tensor-core path and at most %d sequences",
@@ -362,6 +447,7 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
     sp.head_dim = static_cast<int>(headdim); sp.page = static_cast<int>(page_block_size);
     sp.seqlen_q = static_cast<int>(seqlen_q); sp.causal = causal ? 1 : 0;
     sp.num_blocks = num_blocks; sp.scale_log2 = scale_log2; sp.len_add = len_add;
+    sp.err = status;
     const int vec = static_cast<int>(headdim / 32) * 2;  // bytes per lane load
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_cache) |
          reinterpret_cast<uintptr_t>(v_cache)) % vec != 0)
@@ -377,8 +463,9 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
   const fd::WorkspaceLayout wl = fd::workspace_layout(nb_max, num_heads_k, qrows, sms);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (ws == nullptr) {
-    ws = static_cast<uint8_t*>(internal_workspace(dev, wl.total, st));
-    if (ws == nullptr) return set_error(FD_ERR_WORKSPACE, "cannot allocate %zu-byte workspace", wl.total);
+    const char* why = "";
+    ws = static_cast<uint8_t*>(internal_workspace(dev, wl.total, st, &why));
+    if (ws == nullptr) return set_error(FD_ERR_WORKSPACE, "%zu-byte workspace: %s", wl.total, why);
   } else if (workspace_bytes < wl.total) {
     return set_error(FD_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes,
                      wl.total);
@@ -450,12 +537,13 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
     p.page = static_cast<int>(page_block_size);
     p.chunk = chunk;
     p.scale_log2 = scale_log2;
-    p.err = reinterpret_cast<int*>(ws + wl.err_off);
-    p.tickets = reinterpret_cast<uint32_t*>(ws + wl.tickets_off);
+    p.err = status;
+    p.tickets = reinterpret_cast<unsigned long long*>(ws + wl.tickets_off);
     p.part_lse = reinterpret_cast<float*>(ws + wl.lse_off);
     p.part_o = reinterpret_cast<float*>(ws + wl.o_off);
     p.timeout_ns = timeout_ns();
-    p.epoch_word = reinterpret_cast<uint32_t*>(ws + wl.epoch_off);
+    p.epoch_word = reinterpret_cast<unsigned long long*>(ws + wl.epoch_off);
+    p.num_blocks = num_blocks;
     p.cost_tile = cost_tile();
     p.cost_seg = cost_seg();
     p.xworld = 0;
@@ -473,7 +561,7 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
       const cudaError_t ez = cudaMemsetAsync(p.xdone, 0, sizeof(uint32_t), st);
       if (ez != cudaSuccess) return set_error(FD_ERR_CUDA, "clear done counter: %s", cudaGetErrorString(ez));
     }
-    if (err_word != nullptr) *err_word = p.err;
+    if (err_word != nullptr) *err_word = status;
     const int64_t work_bound = nb * num_heads_k * tiles_bound;
     const int grid = static_cast<int>(work_bound < sms ? work_bound : sms);
     const cudaError_t e = fd::launch_decode_sm100(maps, p, dtype, out_fp32, grid, st);
@@ -634,6 +722,13 @@ int fd_append_kv_paged(const void* k_new, const void* v_new, void* k_cache, void
   ap.num_heads_k = static_cast<int>(num_heads_k); ap.head_dim = static_cast<int>(headdim);
   ap.page = static_cast<int>(page_block_size); ap.elem_bytes = esize(dtype);
   ap.skipped = nullptr;
+  {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+      return set_error(FD_ERR_CUDA, "no current CUDA device");
+    ap.err = status_word(dev);
+    if (ap.err == nullptr) return set_error(FD_ERR_CUDA, "cannot find the device status word");
+  }
   ap.k_scale = nullptr;
   ap.v_scale = nullptr;
   const cudaError_t e = fd::launch_append_kv(ap, static_cast<cudaStream_t>(stream));
@@ -731,8 +826,10 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
                            size_t workspace_bytes, void* stream,
                            const ExchangeArgs* xa = nullptr, int** err_word = nullptr) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices)
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return set_error(FD_ERR_CUDA, "no current CUDA device");
+  int* status = status_word(dev);
+  if (status == nullptr) return set_error(FD_ERR_CUDA, "cannot find the device status word");
   if (xa != nullptr && batch_size > fd::kMaxBatchPerLaunch)
     return set_error(FD_ERR_UNSUPPORTED, "cross-GPU exchange takes at most %d sequences",
                      fd::kMaxBatchPerLaunch);
@@ -746,8 +843,9 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
   const fd::WorkspaceLayout wl = fd::workspace_layout(nb_max, num_heads_k, qrows, sms);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (ws == nullptr) {
-    ws = static_cast<uint8_t*>(internal_workspace(dev, wl.total, st));
-    if (ws == nullptr) return set_error(FD_ERR_WORKSPACE, "cannot allocate %zu-byte workspace", wl.total);
+    const char* why = "";
+    ws = static_cast<uint8_t*>(internal_workspace(dev, wl.total, st, &why));
+    if (ws == nullptr) return set_error(FD_ERR_WORKSPACE, "%zu-byte workspace: %s", wl.total, why);
   } else if (workspace_bytes < wl.total) {
     return set_error(FD_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, wl.total);
   } else if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) {
@@ -791,12 +889,13 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
     p.page = static_cast<int>(page_block_size);
     p.chunk = chunk;
     p.scale_log2 = softmax_scale * 1.4426950408889634f;
-    p.err = reinterpret_cast<int*>(ws + wl.err_off);
-    p.tickets = reinterpret_cast<uint32_t*>(ws + wl.tickets_off);
+    p.err = status;
+    p.tickets = reinterpret_cast<unsigned long long*>(ws + wl.tickets_off);
     p.part_lse = reinterpret_cast<float*>(ws + wl.lse_off);
     p.part_o = reinterpret_cast<float*>(ws + wl.o_off);
     p.timeout_ns = timeout_ns();
-    p.epoch_word = reinterpret_cast<uint32_t*>(ws + wl.epoch_off);
+    p.epoch_word = reinterpret_cast<unsigned long long*>(ws + wl.epoch_off);
+    p.num_blocks = num_blocks;
     p.cost_tile = cost_tile(true);
     p.cost_seg = cost_seg(true);
     p.xworld = 0;
@@ -817,7 +916,7 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
       const cudaError_t ez = cudaMemsetAsync(p.xdone, 0, sizeof(uint32_t), st);
       if (ez != cudaSuccess) return set_error(FD_ERR_CUDA, "clear done counter: %s", cudaGetErrorString(ez));
     }
-    if (err_word != nullptr) *err_word = p.err;
+    if (err_word != nullptr) *err_word = status;
     const int64_t work_bound = nb * num_heads_k * tiles_bound;
     const int grid = static_cast<int>(work_bound < sms ? work_bound : sms);
     const cudaError_t e = fd::launch_decode_sm100_kv8(maps, p, q_dtype, out_dtype == FD_DTYPE_FP32, grid, st);
@@ -892,6 +991,13 @@ int fd_append_kv_paged_fp8(const void* k_new, const void* v_new, void* k_cache, 
   ap.num_heads_k = static_cast<int>(num_heads_k); ap.head_dim = static_cast<int>(headdim);
   ap.page = static_cast<int>(page_block_size); ap.elem_bytes = 1;
   ap.skipped = nullptr;
+  {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+      return set_error(FD_ERR_CUDA, "no current CUDA device");
+    ap.err = status_word(dev);
+    if (ap.err == nullptr) return set_error(FD_ERR_CUDA, "cannot find the device status word");
+  }
   ap.k_scale = k_scale;
   ap.v_scale = v_scale;
   const cudaError_t e = fd::launch_append_kv_e4m3(ap, src_dtype, static_cast<cudaStream_t>(stream));
@@ -1015,25 +1121,37 @@ int fd_selftest_bounded_wait(uint64_t budget_ns, uint64_t* waited_ns) {
 
 int fd_device_status(void) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices)
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return set_error(FD_ERR_CUDA, "no current CUDA device");
   if (cudaDeviceSynchronize() != cudaSuccess)
     return set_error(FD_ERR_CUDA, "device synchronize failed");
-  void* ws = nullptr;
-  {
-    std::lock_guard<std::mutex> lk(g_dev[dev].mu);
-    ws = g_dev[dev].ws;
-  }
-  if (ws == nullptr) return set_ok();
+  int* w = status_word(dev);
+  if (w == nullptr) return set_error(FD_ERR_CUDA, "cannot find the device status word");
   int word = 0;
-  if (cudaMemcpy(&word, ws, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+  if (cudaMemcpy(&word, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
     return set_error(FD_ERR_CUDA, "cannot read device status");
-  if (word != 0) {
-    const int zero = 0;
-    cudaMemcpy(ws, &zero, sizeof(int), cudaMemcpyHostToDevice);
-    return set_error(FD_ERR_DEVICE_TIMEOUT, "device reported status %d", word);
-  }
-  return set_ok();
+  if (word == 0) return set_ok();
+  const int zero = 0;
+  if (cudaMemcpy(w, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
+    return set_error(FD_ERR_CUDA, "cannot clear device status");
+  if (word == FD_ERR_BAD_PAGE)
+    return set_error(FD_ERR_BAD_PAGE,
+                     "a block_table entry inside a sequence's length was outside [0, num_blocks) "
+                     "(those rows were read as zeros)");
+  if (word == FD_ERR_DEVICE_TIMEOUT)
+    return set_error(FD_ERR_DEVICE_TIMEOUT, "a bounded in-kernel wait ran out");
+  return set_error(word, "device reported status %d", word);
+}
+
+size_t fd_library_workspace_bytes(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+  DeviceState& s = g_dev[dev];
+  std::lock_guard<std::mutex> lk(s.mu);
+  size_t total = 0;
+  for (const StreamWorkspace& w : s.ws) total += w.bytes;
+  for (const StreamWorkspace& w : s.retired) total += w.bytes;
+  return total;
 }
 
 }  // extern "C"

@@ -21,6 +21,7 @@
 
 #include "fd_fp8.cuh"
 #include "fd_kernels.h"
+#include "fd_ptx.cuh"
 
 namespace fd {
 
@@ -43,6 +44,8 @@ __global__ void __launch_bounds__(kAppendThreads)
   if (page_idx < p.bt_stride) pg = p.block_table[static_cast<int64_t>(b) * p.bt_stride + page_idx];
   if (pg < 0 || pg >= p.num_blocks) {
     if (threadIdx.x == 0 && p.skipped != nullptr) atomicAdd(p.skipped, 1);
+    // a page id in the table that is not in the pool is the caller's error
+    if (threadIdx.x == 0 && page_idx < p.bt_stride) report_status(p.err, kStatusBadPage);
     return;
   }
   const int64_t row_bytes = static_cast<int64_t>(p.num_heads_k) * p.head_dim * p.elem_bytes;
@@ -86,6 +89,8 @@ __global__ void __launch_bounds__(kAppendThreads)
   if (page_idx < p.bt_stride) pg = p.block_table[static_cast<int64_t>(b) * p.bt_stride + page_idx];
   if (pg < 0 || pg >= p.num_blocks) {
     if (threadIdx.x == 0 && p.skipped != nullptr) atomicAdd(p.skipped, 1);
+    // a page id in the table that is not in the pool is the caller's error
+    if (threadIdx.x == 0 && page_idx < p.bt_stride) report_status(p.err, kStatusBadPage);
     return;
   }
   const int64_t row_elems = static_cast<int64_t>(p.num_heads_k) * p.head_dim;

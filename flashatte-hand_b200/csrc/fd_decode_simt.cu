@@ -8,7 +8,9 @@
 // (sequence, query head), same edge rules (length <= 0 writes zeros, length 1
 // returns the single V row), but warp-parallel over tokens instead of one
 // block reduction per token, any head dim in {32, 64, 128, 256}, any group
-// size and page size, fp32 online softmax in the log2 domain.
+// size and page size, fp32 online softmax in the log2 domain.  A page id
+// inside a sequence's range that is outside the pool reads as zero rows and
+// is reported in the device status word (FD_ERR_BAD_PAGE).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -79,6 +81,7 @@ __global__ void __launch_bounds__(32 * kSimtWarps)
   for (int t = warp; t < len; t += kSimtWarps) {
     const int64_t page = bt[t / p.page];
     const bool in_pool = page >= 0 && page < p.num_blocks;  // out-of-pool ids read as zero rows
+    if (!in_pool && lane == 0) report_status(p.err, kStatusBadPage);
     const int64_t row = ((page * p.page + (t % p.page)) * p.num_heads_k + kvh) * D + lane * VEC;
     Vec<T, VEC> kv, vv;
     if (in_pool) {

@@ -14,11 +14,10 @@ WorkspaceLayout workspace_layout(int64_t batch_per_launch, int64_t num_heads_k, 
   const size_t pairs = static_cast<size_t>(batch_per_launch * num_heads_k);
   const size_t slots = pairs + static_cast<size_t>(grid_max);
   WorkspaceLayout w;
-  w.err_off = 0;
-  w.epoch_off = 64;  // two words, see DecodeParams::epoch_word
-  w.done_off = 128;
-  w.tickets_off = 256;
-  w.lse_off = w.tickets_off + up(pairs * 4);
+  w.epoch_off = 0;     // two 64-bit words, see DecodeParams::epoch_word
+  w.done_off = 64;     // cross-GPU exchange: finished-CTA count
+  w.tickets_off = 128; // one 64-bit arrival counter per (sequence, KV head) pair
+  w.lse_off = up(w.tickets_off + pairs * 8);
   w.o_off = w.lse_off + up(slots * qrows * 4);
   w.total = w.o_off + up(slots * qrows * kHeadDim * 4);
   return w;

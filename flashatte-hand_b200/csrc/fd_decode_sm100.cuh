@@ -109,22 +109,30 @@ template <bool KV8, int NCOL = kMaxGroup> struct Geo {
 constexpr int kQkWarp = 7;  // issues QK; warp 1 issues PV
 constexpr int kVProducerWarp = 6;
 
-// Arrival counter of a split (sequence, KV head) pair: bits [12, 32) hold the
-// launch epoch, bits [0, 12) the arrivals seen in that epoch.  A counter left
-// by any earlier launch (even one that stopped early) reads as zero, so the
-// workspace never needs clearing.  Returns true for the pair's last arrival.
-// The first arrival of a launch stamps the epoch with one compare-and-swap;
-// every arrival that sees the stamp counts itself with one fetch-and-add, so
-// the tens of CTAs sharing one long sequence's pair, finishing together, do
-// not queue on a compare-and-swap loop.
-__device__ __forceinline__ bool ticket_arrive(uint32_t* t, uint32_t epoch, int nseg) {
-  uint32_t cur = *reinterpret_cast<volatile uint32_t*>(t);
+// Arrival counter of a split (sequence, KV head) pair, and of the grid:
+// bits [12, 64) hold the launch epoch, bits [0, 12) the arrivals seen in that
+// epoch (at most one per CTA, and a launch has at most 4095 CTAs).  Epochs run
+// 1 .. 2^52 - 1 and then start again at 1, so a counter can only be mistaken
+// for the current launch's after 2^52 - 1 launches on one workspace (centuries
+// of back-to-back calls).  Only a launch that stopped early (a bounded wait
+// ran out) leaves a counter behind: the CTA that merges a pair clears its
+// counter and the last CTA to arrive clears the grid counter, so a launch
+// that completes leaves every counter at zero.  The first arrival of a launch
+// stamps the epoch with one compare-and-swap; every arrival that sees the
+// stamp counts itself with one fetch-and-add, so the tens of CTAs sharing one
+// long sequence's pair, finishing together, do not queue on a compare-and-swap
+// loop.  Returns true for the pair's last arrival.
+constexpr int kTicketCountBits = 12;
+constexpr unsigned long long kTicketCountMask = (1ull << kTicketCountBits) - 1ull;
+constexpr unsigned long long kEpochMax = (1ull << (64 - kTicketCountBits)) - 1ull;
+__device__ __forceinline__ bool ticket_arrive(unsigned long long* t, unsigned long long epoch, int nseg) {
+  unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(t);
   for (;;) {
-    if ((cur >> 12) == epoch) {
-      const uint32_t old = atomicAdd(t, 1u);
-      return (old & 0xFFFu) + 1u == static_cast<uint32_t>(nseg);
+    if ((cur >> kTicketCountBits) == epoch) {
+      const unsigned long long old = atomicAdd(t, 1ull);
+      return (old & kTicketCountMask) + 1ull == static_cast<unsigned long long>(nseg);
     }
-    const uint32_t prev = atomicCAS(t, cur, (epoch << 12) | 1u);
+    const unsigned long long prev = atomicCAS(t, cur, (epoch << kTicketCountBits) | 1ull);
     if (prev == cur) return nseg == 1;
     cur = prev;
   }
@@ -465,7 +473,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   // Tiles of this CTA, published by the producer once its walk is done.
   volatile int* tiles_total = reinterpret_cast<volatile int*>(smem + G::kOffMisc + 12);
   // This launch's epoch (see DecodeParams::epoch_word), read once by thread 0.
-  uint32_t* launch_epoch = reinterpret_cast<uint32_t*>(smem + G::kOffMisc + 16);
+  unsigned long long* launch_epoch = reinterpret_cast<unsigned long long*>(smem + G::kOffMisc + 16);
   float* red = reinterpret_cast<float*>(smem + G::kOffRed);
   float* fin = reinterpret_cast<float*>(smem + G::kOffFin);
   float* qinv_ring = reinterpret_cast<float*>(smem + G::kOffQInv);
@@ -525,8 +533,8 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   pdl_wait_prerequisites();
   // The epoch load is issued here and consumed after the sequence lengths'
   // loads, so the two round trips overlap.
-  uint32_t epoch_ld = 0;
-  if (tid == 0) epoch_ld = *reinterpret_cast<volatile uint32_t*>(p.epoch_word);
+  unsigned long long epoch_ld = 0;
+  if (tid == 0) epoch_ld = *reinterpret_cast<volatile unsigned long long*>(p.epoch_word);
   for (int b = tid; b < batch; b += kSm100Threads) {
     const int stored = __ldg(p.seqlens + b);
     // keys cached before this step plus the ones it appended
@@ -538,7 +546,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   }
   if (tid == 0) {
     prefix[0] = 0;
-    *launch_epoch = epoch_ld & 0xFFFFFu;
+    *launch_epoch = epoch_ld & kEpochMax;
   }
   fence_proxy_async_smem();
   tc_fence_before();
@@ -660,6 +668,14 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         const bool need = lane < nbox;
         int page_id = 0;
         if (need) page_id = __ldg(bt_row + pos / p.page);  // issued before the wait
+        if (need && (page_id < 0 || page_id >= p.num_blocks)) {
+          // A page id inside the sequence's range that is not in the pool:
+          // report it and fetch a box that lies wholly past the pool instead,
+          // which the tensor copy fills with zeros (no access outside the
+          // cache; those keys score 0 and their values add 0).
+          report_status(p.err, kStatusBadPage);
+          page_id = static_cast<int>(p.num_blocks);
+        }
         const int stage = static_cast<int>(it % G::kStages);
         ok = lane0_wait(&ring_empty[stage], static_cast<uint32_t>((it / G::kStages) & 1) ^ 1u,
                         abort_flag, budget, lane);
@@ -717,13 +733,17 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     if (!is_v && lane == 0) {
       *tiles_total = static_cast<int>(it);
       // Every CTA has read this launch's epoch before it counts itself here;
-      // the last to count hands the next launch a new one (1 .. 2^20-1; a
-      // zeroed workspace starts at 0, consistent with its zeroed counters),
-      // which that launch reads only after this grid has completed.  Done
-      // after the last load is issued, the round trips overlap the drain of
-      // the ring, and CTAs arrive spread over their different finishing times.
-      const uint32_t e = *launch_epoch;
-      if (ticket_arrive(p.epoch_word + 1, e, static_cast<int>(gridDim.x))) p.epoch_word[0] = e % 0xFFFFFu + 1u;
+      // the last to count hands the next launch a new one (1 .. 2^52 - 1; a
+      // zeroed workspace starts at 0, consistent with its zeroed counters)
+      // and clears the count; the next launch reads both only after this
+      // grid has completed.  Done after the last load is issued, the round
+      // trips overlap the drain of the ring, and CTAs arrive spread over
+      // their different finishing times.
+      const unsigned long long e = *launch_epoch;
+      if (ticket_arrive(p.epoch_word + 1, e, static_cast<int>(gridDim.x))) {
+        p.epoch_word[0] = e % kEpochMax + 1ull;
+        p.epoch_word[1] = 0ull;
+      }
     }
   } else if (warp == 1 || warp == kQkWarp) {
     // ---------------------------------------------------------- UMMA issuers
@@ -981,6 +1001,9 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       if (d == 0) {
         int is_last = 0;
         if (!*abort_flag) is_last = ticket_arrive(p.tickets + sg.pair, *launch_epoch, sg.nseg) ? 1 : 0;
+        // Every segment of the pair has counted itself: clear the counter for
+        // later launches (nothing else touches it in this one).
+        if (is_last) *reinterpret_cast<volatile unsigned long long*>(p.tickets + sg.pair) = 0ull;
         *last_flag = is_last;
       }
       named_bar_sync(1, 128);
@@ -1272,7 +1295,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   }
   if (*abort_flag) {
     if (tid == 0) {
-      atomicExch(p.err, 5);
+      report_status(p.err, kStatusTimeout);
       // Let any copy or MMA still in flight land before the CTA's shared
       // memory and TMEM are released (bounded: 2 ms).
       const uint64_t t0 = globaltimer_ns();

@@ -29,14 +29,19 @@ struct DecodeParams {
   float scale_log2;           // softmax_scale * log2(e)
   float* part_o;              // [slots, group, 128] fp32 (normalised partial O)
   float* part_lse;            // [slots, group] log2-domain partial LSE
-  uint32_t* tickets;          // [batch * num_heads_k] epoch-tagged arrival counters
-  int* err;                   // device error word
+  // [batch * num_heads_k] arrival counters of split pairs: bits [12, 64) the
+  // launch epoch, bits [0, 12) the arrivals seen in it.  The CTA that merges
+  // a pair clears its counter, so a launch that completes leaves them all 0.
+  unsigned long long* tickets;
+  int* err;                   // the device's status word (first error a kernel met)
   unsigned long long timeout_ns;
   // Launch epoch kept on the device (workspace): [0] the epoch the next
-  // launch uses, [1] the launch's epoch-tagged count of CTAs that have read
-  // it; the last of them advances [0].  A launch replayed from a CUDA graph
-  // therefore gets a fresh epoch like any other launch.
-  uint32_t* epoch_word;
+  // launch uses (1 .. 2^52 - 1; 0 in a zeroed workspace), [1] the launch's
+  // epoch-tagged count of CTAs that have read it; the last of them advances
+  // [0] and clears [1].  A launch replayed from a CUDA graph therefore gets a
+  // fresh epoch like any other launch.
+  unsigned long long* epoch_word;
+  int64_t num_blocks;         // pages in the K/V pool: block_table ids must lie in [0, num_blocks)
   // Cross-GPU split-KV exchange (xworld > 0): instead of out/lse, every
   // result row goes as fp32 O and ln-LSE to each rank's exchange part
   // xpart[j] (O at [row*128 + d], LSE at [xlse_off + lse row]); the CTA that
@@ -69,6 +74,7 @@ struct SimtParams {
   int64_t num_blocks;
   float scale_log2;
   int len_add;  // as DecodeParams::len_add
+  int* err;     // the device's status word (FD_ERR_BAD_PAGE on an out-of-pool page id)
 };
 
 // New keys/values written into the paged cache before attention
@@ -81,6 +87,7 @@ struct AppendParams {
   int64_t bt_stride, num_blocks;
   int batch, seqlen_new, num_heads_k, head_dim, page, elem_bytes;
   int* skipped;  // nullable: incremented per (b, t) row that had no page to go to
+  int* err;      // the device's status word (FD_ERR_BAD_PAGE on an out-of-pool page id)
   const float* k_scale;  // e4m3 cache only: per-KV-head quantisation scales
   const float* v_scale;
 };
@@ -88,9 +95,11 @@ cudaError_t launch_append_kv(const AppendParams& p, cudaStream_t stream);
 // 16-bit new rows (src_dtype 0 bf16, 1 fp16) into an e4m3 cache: x / scale[h], head_dim % 8 == 0.
 cudaError_t launch_append_kv_e4m3(const AppendParams& p, int src_dtype, cudaStream_t stream);
 
-// Workspace carve-up for the tensor-core kernel.
+// Workspace carve-up for the tensor-core kernel: [epoch_off, lse_off) must
+// be zero before the workspace's first use (the kernel keeps it consistent
+// afterwards); the partials after it need no initial value.
 struct WorkspaceLayout {
-  size_t err_off, epoch_off, done_off, tickets_off, lse_off, o_off, total;
+  size_t epoch_off, done_off, tickets_off, lse_off, o_off, total;
 };
 WorkspaceLayout workspace_layout(int64_t batch_per_launch, int64_t num_heads_k, int64_t qrows,
                                  int grid_max);
@@ -137,6 +146,19 @@ cudaError_t launch_bounded_wait_probe(unsigned long long budget_ns, int* status,
                                       unsigned long long* waited_ns, cudaStream_t stream);
 
 size_t sm100_smem_bytes();
+
+// Device status word codes (match FD_ERR_DEVICE_TIMEOUT / FD_ERR_BAD_PAGE).
+constexpr int kStatusTimeout = 5;
+constexpr int kStatusBadPage = 6;
+
+// Address of the current device's status word (a __device__ int inside this
+// library, looked up once per device); nullptr if the lookup failed.
+int* device_status_word();
+
+// Whether a 16-bit decode of this shape runs on the tensor-core kernel (and so
+// uses split scratch) rather than the CUDA-core kernel, which needs none.
+bool uses_tensor_core_path(const void* q, const void* k_cache, const void* v_cache,
+                           int64_t headdim, int64_t qrows, int64_t page_block_size);
 
 // Record `code` and a printf-style message as this thread's last error (what
 // fd_last_error / fd_last_error_message report) and return `code`.

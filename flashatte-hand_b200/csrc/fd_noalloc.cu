@@ -13,7 +13,9 @@
 // (kNoAllocScratchBytes per GPU that loads the library, held until the
 // process exits).  Host code cannot use the array's name as a device
 // address, so the first call on each device looks the address up with
-// cudaGetSymbolAddress while that device is current and keeps it.
+// cudaGetSymbolAddress while that device is current and keeps it.  Errors a
+// kernel meets are reported in the device status word that fd_device_status
+// reads, as for every other entry point.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -56,27 +58,36 @@ extern "C" int fd_decode_paged_noalloc(const void* q, const void* k_cache, const
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return fd::report_error(FD_ERR_CUDA, "no current CUDA device");
-  const size_t need = fd_decode_workspace_size(batch_size, num_heads, num_heads_k, headdim);
-  if (need > kNoAllocScratchBytes)
-    return fd::report_error(FD_ERR_WORKSPACE,
-                            "this shape needs %zu bytes of split scratch; the no-allocation entry "
-                            "point has a fixed %zu-byte area (use fd_decode_paged with a caller "
-                            "workspace instead)",
-                            need, kNoAllocScratchBytes);
   cudaError_t status = cudaSuccess;
   void* scratch = scratch_address(dev, &status);
   if (scratch == nullptr)
     return fd::report_error(FD_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s",
                             cudaGetErrorString(status));
-  // Every call shares the area and finds the previous call's contents: clear
-  // the part that must start at zero (device error word, arrival counters).
-  if (need > 0) {
-    const size_t head = fd::workspace_layout(
-        batch_size < fd::kMaxBatchPerLaunch ? batch_size : fd::kMaxBatchPerLaunch, num_heads_k,
-        num_heads / num_heads_k, 0).lse_off;
-    const cudaError_t e = cudaMemsetAsync(scratch, 0, head, static_cast<cudaStream_t>(stream));
-    if (e != cudaSuccess)
-      return fd::report_error(FD_ERR_CUDA, "clearing scratch: %s", cudaGetErrorString(e));
+  // Shapes the CUDA-core kernel takes use no split scratch at all: they are
+  // never refused for its size.  (Invalid arguments are left to
+  // fd_decode_paged to report.)
+  const bool uses_scratch =
+      num_heads > 0 && num_heads_k > 0 && num_heads % num_heads_k == 0 &&
+      fd::uses_tensor_core_path(q, k_cache, v_cache, headdim, num_heads / num_heads_k,
+                                page_block_size);
+  if (uses_scratch) {
+    const size_t need = fd_decode_workspace_size(batch_size, num_heads, num_heads_k, headdim);
+    if (need > kNoAllocScratchBytes)
+      return fd::report_error(FD_ERR_WORKSPACE,
+                              "this shape needs %zu bytes of split scratch; the no-allocation entry "
+                              "point has a fixed %zu-byte area (use fd_decode_paged with a caller "
+                              "workspace instead)",
+                              need, kNoAllocScratchBytes);
+    // Every call shares the area and finds the previous call's contents: clear
+    // the part that must start at zero (launch epoch and arrival counters).
+    if (need > 0) {
+      const size_t head = fd::workspace_layout(
+          batch_size < fd::kMaxBatchPerLaunch ? batch_size : fd::kMaxBatchPerLaunch, num_heads_k,
+          num_heads / num_heads_k, 0).lse_off;
+      const cudaError_t e = cudaMemsetAsync(scratch, 0, head, static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess)
+        return fd::report_error(FD_ERR_CUDA, "clearing scratch: %s", cudaGetErrorString(e));
+    }
   }
   return fd_decode_paged(q, k_cache, v_cache, out, lse, cache_seqlens, block_table,
                          block_table_stride, batch_size, num_heads, num_heads_k, headdim,

@@ -244,6 +244,12 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* addr) {
 }
 
 // ---------------------------------------------------------------- misc
+// Record `code` in the device status word unless an earlier error is there
+// (the first error a kernel meets is the one the host reads back).
+__device__ __forceinline__ void report_status(int* word, int code) {
+  if (word != nullptr) atomicCAS(word, 0, code);
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

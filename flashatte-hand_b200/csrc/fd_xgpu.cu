@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(kCombineThreads)
       while (ld_acquire_sys_u32(flags + j) != epoch) {
         if (globaltimer_ns() - t0 > timeout_ns) {
           ok = 0;
-          atomicExch(err, 5);
+          report_status(err, kStatusTimeout);
           break;
         }
       }

@@ -5,8 +5,8 @@ Put the ``flashatte-hand_b200`` directory on ``sys.path`` and
 ``import flashdecode``.
 """
 from ._lib import FlashDecodeError, LIB_PATH, load_library
-from .ops import (append_kv, combine_lse, device_status, flash_decode, last_error, run_kernel,
-                  workspace_size)
+from .ops import (DecodePlan, append_kv, combine_lse, device_status, flash_decode, last_error,
+                  run_kernel, workspace_size)
 
-__all__ = ["FlashDecodeError", "LIB_PATH", "load_library", "append_kv", "combine_lse", "device_status",
-           "flash_decode", "last_error", "run_kernel", "workspace_size"]
+__all__ = ["FlashDecodeError", "LIB_PATH", "load_library", "DecodePlan", "append_kv", "combine_lse",
+           "device_status", "flash_decode", "last_error", "run_kernel", "workspace_size"]

@@ -50,6 +50,7 @@ SIGNATURES: dict[str, tuple] = {
     "fd_error_string": (_c.c_char_p, [_i32]),
     "fd_last_error_message": (_c.c_char_p, []),
     "fd_device_status": (_i32, []),
+    "fd_library_workspace_bytes": (_sz, []),
     "fd_selftest_bounded_wait": (_i32, [_c.c_uint64, _c.POINTER(_c.c_uint64)]),
     "fd_version": (_c.c_char_p, []),
 }
@@ -57,7 +58,8 @@ SIGNATURES: dict[str, tuple] = {
 FD_DTYPE_BF16, FD_DTYPE_FP16, FD_DTYPE_FP32, FD_DTYPE_E4M3 = 0, 1, 2, 3
 FD_OK = 0
 STATUS_NAMES = {0: "FD_OK", 1: "FD_ERR_INVALID_ARG", 2: "FD_ERR_UNSUPPORTED",
-                3: "FD_ERR_WORKSPACE", 4: "FD_ERR_CUDA", 5: "FD_ERR_DEVICE_TIMEOUT"}
+                3: "FD_ERR_WORKSPACE", 4: "FD_ERR_CUDA", 5: "FD_ERR_DEVICE_TIMEOUT",
+                6: "FD_ERR_BAD_PAGE"}
 
 _lib = None
 

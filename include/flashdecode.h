@@ -37,6 +37,9 @@ extern "C" {
 #define FD_ERR_WORKSPACE 3      /* workspace missing or too small            */
 #define FD_ERR_CUDA 4           /* a CUDA runtime/driver call failed         */
 #define FD_ERR_DEVICE_TIMEOUT 5 /* a bounded in-kernel wait ran out          */
+#define FD_ERR_BAD_PAGE 6       /* a block_table id inside a sequence's range
+                                   lies outside [0, num_blocks) (reported by
+                                   fd_device_status; those rows read as 0)   */
 
 /*
  * run_kernel - drop-in for the reference operator surface.
@@ -77,14 +80,24 @@ void run_kernel(const void* q, const void* k_cache_paged, const void* v_cache_pa
  * out_dtype:    FD_DTYPE_FP32 or the value of dtype.
  * max_seqlen_k: upper bound on cache_seqlens (0 = unknown); only sizes the grid.
  * workspace:    device buffer of at least fd_decode_workspace_size(...) bytes,
- *               any contents (it needs no clearing: counters in it are
- *               tagged with a per-launch epoch that the kernel keeps in the
- *               workspace), or NULL to use a library-owned per-device buffer
- *               (allocated on first use: make one call before capturing a
- *               CUDA graph, or pass a workspace).  One workspace must not be
- *               used by two calls that can run at the same time.
+ *               zero-filled once before its first use (cudaMemset); the
+ *               kernel keeps it consistent from then on (its counters carry a
+ *               per-launch epoch and are cleared when a launch completes), so
+ *               it never needs clearing again, also after a call that
+ *               reported FD_ERR_DEVICE_TIMEOUT.  Or NULL: the library then
+ *               uses a buffer of its own for this (device, stream) pair,
+ *               allocated and zero-filled on the stream's first call and kept
+ *               until the process exits, so calls on different streams never
+ *               share one.  It grows to the largest shape the stream has
+ *               seen; an outgrown buffer is kept too (a CUDA graph captured
+ *               on the stream may still use it).  A call being captured into
+ *               a CUDA graph may allocate it (the allocation is made outside
+ *               the graph).  One workspace must not be used by two calls
+ *               that can run at the same time.
  * stream:       cudaStream_t (NULL = legacy default stream).
- * Returns FD_OK or an FD_ERR_* code; launches are asynchronous.
+ * Returns FD_OK or an FD_ERR_* code; launches are asynchronous.  Errors met
+ * inside a kernel (a bounded wait that ran out, a block_table id outside the
+ * pool) are reported later by fd_device_status.
  */
 int fd_decode_paged(const void* q, const void* k_cache, const void* v_cache, void* out, float* lse,
                     const int32_t* cache_seqlens, const int32_t* block_table,
@@ -174,7 +187,8 @@ int fd_decode_paged_kvappend(const void* q, void* k_cache, void* v_cache, const 
  * keys; pass NULL for both otherwise.  Supported: head dim 128,
  * seqlen_q * (Hq / Hkv) <= 16, page a multiple of 16, 16-byte aligned
  * q / caches (FD_ERR_UNSUPPORTED otherwise).  Workspace: at least
- * fd_decode_workspace_size_fp8(...) bytes, 256-byte aligned, or NULL.
+ * fd_decode_workspace_size_fp8(...) bytes, 256-byte aligned and zero-filled
+ * before its first use, or NULL (as for fd_decode_paged).
  */
 int fd_decode_paged_fp8(const void* q, void* k_cache, void* v_cache, const float* k_scale,
                         const float* v_scale, const void* k_new, const void* v_new,
@@ -217,7 +231,11 @@ int fd_append_kv_paged_fp8(const void* k_new, const void* v_new, void* k_cache, 
  * array's device address (cudaGetSymbolAddress, that device current), so make
  * that first call before any stream capture.  All calls share the array and
  * it keeps the previous call's contents (the call clears what must start at
- * zero): calls that can overlap on the GPU race with each other.
+ * zero): calls that can overlap on the GPU race with each other.  Shapes the
+ * CUDA-core kernel takes (head dim other than 128, more than 16 query heads
+ * per KV head, pages not a multiple of 16, q/k/v not 16-byte aligned) use no
+ * scratch and are never refused for its size.  Kernel-side errors are read
+ * with fd_device_status, as for fd_decode_paged.
  * No counterpart in the reference, whose run_kernel always cudaMallocs its
  * split workspace on first use.
  */
@@ -313,12 +331,26 @@ const char* fd_error_string(int code);
 const char* fd_last_error_message(void);
 
 /*
- * fd_device_status - read and clear the device-side error word of the
- * library-owned workspace of the current device (FD_ERR_DEVICE_TIMEOUT if a
- * bounded wait inside a kernel ran out since the last read).  Synchronises
- * the current device.
+ * fd_device_status - read and clear the current device's status word: the
+ * first error a kernel of this library met there since the last read,
+ * whatever entry point and workspace the call used.  FD_ERR_DEVICE_TIMEOUT:
+ * a bounded in-kernel wait ran out (that call's results are incomplete);
+ * FD_ERR_BAD_PAGE: a block_table entry inside a sequence's length was
+ * outside [0, num_blocks) (its rows were read as zeros, nothing outside the
+ * cache was touched).  FD_OK otherwise.  Synchronises the current device.
+ * Replaces: nothing in the reference, whose kernels report no errors and
+ * gather through block_table unchecked (best :741-742).
  */
 int fd_device_status(void);
+
+/*
+ * fd_library_workspace_bytes - bytes of workspace the library holds on the
+ * current device for calls that passed workspace = NULL (all streams,
+ * outgrown buffers included).
+ * Replaces: nothing in the reference (its workspace is one process-global
+ * buffer, best :17-20); lets a caller account for the library's memory.
+ */
+size_t fd_library_workspace_bytes(void);
 
 /*
  * fd_selftest_bounded_wait - launch a one-warp kernel that waits on an

@@ -37,6 +37,7 @@ def test_version_and_error_strings(lib):
     assert lib.fd_version().decode().startswith("flashdecode-sm100")
     assert lib.fd_error_string(0) == b"ok"
     assert lib.fd_error_string(5) == b"in-kernel wait timed out"
+    assert lib.fd_error_string(6) == b"page id outside the KV pool"
 
 
 def _call(lib, **kw):

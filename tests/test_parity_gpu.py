@@ -162,7 +162,7 @@ def test_batch_larger_than_one_launch():
     c = cases.custom_case("bigbatch", torch.float16, sl, 8, 2, page=16, seed=1)
     t = cases.materialize(c, "cuda", seed=1)
     out, lse = run(t, c, return_softmax_lse=True)
-    check(c, t, out, lse, rows=[0, 1, 511, 512, 1023, 1024, 2047, 2048, 2049, 2499])
+    check(c, t, out, lse)  # every row, across the 512-sequence launch boundaries
 
 
 @pytest.mark.parametrize("shape", cases.CONTEST_SHAPES)
@@ -181,15 +181,19 @@ def test_reference_abi_contest_shapes(shape):
 
 @pytest.mark.parametrize("idx", [1, 2, 3, 4, 5])
 def test_baseline_configs(idx):
-    """Full-size BASELINE configs: sampled rows against the oracle, all rows finite."""
+    """Full-size BASELINE configs: every output row and LSE against the oracle
+    (the reference evaluator's gate is likewise one allclose over the whole
+    output, evaluate_flashattn_submission.py:275-276)."""
     c = cases.config_case(idx)
     t = cases.materialize(c, "cuda")
     out, lse = run(t, c, return_softmax_lse=True)
     torch.cuda.synchronize()
     assert torch.isfinite(out.float()).all() and torch.isfinite(lse).all()
-    order = sorted(range(c.B), key=lambda b: int(c.seqlens[b]))
-    rows = sorted({order[0], order[-1], order[len(order) // 2], 0, c.B - 1})
-    check(c, t, out, lse, rows=rows)
+    # chunks of sequences keep the oracle's host memory bounded (config 4's
+    # two 262144-token sequences are ~2 GB of fp32 K and V each)
+    step = 16 if idx != 4 else 1
+    for r0 in range(0, c.B, step):
+        check(c, t, out, lse, rows=list(range(r0, min(c.B, r0 + step))))
 
 
 def test_combine_lse_matches_oracle_merge():
