@@ -432,12 +432,15 @@ def main():
 
     torch.cuda.set_device(local)
     dist = None
+    own_group = False
     if world > 1:
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        if not dist.is_initialized():  # a caller running several benches may hold one
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+            own_group = True
     full, scaling, parallel, config = plan(args, world)
     lib = flashdecode.load_library()
     stream = torch.cuda.current_stream()
@@ -616,7 +619,7 @@ def main():
 
     if splitter is not None:
         splitter.close()
-    if dist is not None:
+    if own_group:
         dist.destroy_process_group()
     if rank != 0:
         return
