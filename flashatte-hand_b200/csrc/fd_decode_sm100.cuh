@@ -1023,14 +1023,16 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         named_bar_sync(1, 128);
       }
       // A warp covers a 128-dim row with 16-byte loads (lane l: dims 4l..4l+3);
-      // warp w merges rows w, w+4, ...  Each step loads the partial of every
-      // such row for one segment and several steps are in flight, so a pair
-      // cut into tens of segments merges in a few L2 round trips of 16-byte
-      // requests rather than many of 4-byte ones.
+      // warp w merges rows w, w+4, ...  The segments are taken in batches:
+      // each thread issues the loads of a whole batch (8 16-byte loads,
+      // kBatch segments x its kRows rows) before it uses any of them, so a
+      // pair cut into tens of segments (a long sequence spread over many
+      // CTAs) merges in a few L2 round trips.
       auto lse_of = [&](int j, int h) {
         return staged ? sl[j * qrows + h] : __ldcg(p.part_lse + (sbase + j) * qrows + h);
       };
       constexpr int kRows = (NCOL + 3) / 4;  // rows per thread
+      constexpr int kBatch = 8 / kRows;      // segments per batch of loads
       const int lane4 = d & 31, rg = d >> 5;
       float mx[kRows], den[kRows], acc[kRows][4];
 #pragma unroll
@@ -1045,27 +1047,33 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
           if (rg + 4 * k < qrows) mx[k] = fmaxf(mx[k], lse_of(j, rg + 4 * k));
       }
       const float* po4 = p.part_o + sbase * qrows * kHeadDim + 4 * lane4;
-#pragma unroll 4
-      for (int j = 0; j < sg.nseg; ++j) {
-        float4 o[kRows];
+      for (int j0 = 0; j0 < sg.nseg; j0 += kBatch) {
+        float4 o[kBatch][kRows];
 #pragma unroll
-        for (int k = 0; k < kRows; ++k) {
-          const int h = rg + 4 * k;
-          o[k] = h < qrows ? __ldcg(reinterpret_cast<const float4*>(
-                                 po4 + (static_cast<int64_t>(j) * qrows + h) * kHeadDim))
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int u = 0; u < kBatch; ++u) {
+#pragma unroll
+          for (int k = 0; k < kRows; ++k) {
+            const int h = rg + 4 * k, j = j0 + u;
+            o[u][k] = (j < sg.nseg && h < qrows)
+                          ? __ldcg(reinterpret_cast<const float4*>(
+                                po4 + (static_cast<int64_t>(j) * qrows + h) * kHeadDim))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
         }
 #pragma unroll
-        for (int k = 0; k < kRows; ++k) {
-          const int h = rg + 4 * k;
-          if (h < qrows) {
-            const float lj = lse_of(j, h);
-            const float wj = lj == neg_inf ? 0.f : fast_exp2(lj - mx[k]);  // empty parts hold O = 0
-            acc[k][0] = fmaf(wj, o[k].x, acc[k][0]);
-            acc[k][1] = fmaf(wj, o[k].y, acc[k][1]);
-            acc[k][2] = fmaf(wj, o[k].z, acc[k][2]);
-            acc[k][3] = fmaf(wj, o[k].w, acc[k][3]);
-            den[k] += wj;
+        for (int u = 0; u < kBatch; ++u) {
+#pragma unroll
+          for (int k = 0; k < kRows; ++k) {
+            const int h = rg + 4 * k, j = j0 + u;
+            if (j < sg.nseg && h < qrows) {
+              const float lj = lse_of(j, h);
+              const float wj = lj == neg_inf ? 0.f : fast_exp2(lj - mx[k]);  // empty parts hold O = 0
+              acc[k][0] = fmaf(wj, o[u][k].x, acc[k][0]);
+              acc[k][1] = fmaf(wj, o[u][k].y, acc[k][1]);
+              acc[k][2] = fmaf(wj, o[u][k].z, acc[k][2]);
+              acc[k][3] = fmaf(wj, o[u][k].w, acc[k][3]);
+              den[k] += wj;
+            }
           }
         }
       }
