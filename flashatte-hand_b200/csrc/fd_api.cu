@@ -39,6 +39,10 @@ constexpr int kDefaultCostSeg = 12;
 // short sequences overloaded (295 us); these give 198 us.
 constexpr int kDefaultCostTile8 = 8;
 constexpr int kDefaultCostSeg8 = 48;
+// Pair-aligned split (one whole (sequence, KV head) pair per CTA) for
+// launches with no more pairs than SMs and no sequence longer than this
+// many 128-token tiles (see the schedule set-up in fd_decode_sm100.cuh).
+constexpr int kDefaultAlignTiles = 16;
 
 thread_local int t_last_error = FD_OK;
 thread_local char t_last_msg[256] = "ok";
@@ -285,6 +289,11 @@ int cost_seg(bool kv8 = false) {
   static const int v = env_int("FD_COST_SEG", kDefaultCostSeg, 1, 256);
   static const int v8 = env_int("FD_COST_SEG8", kDefaultCostSeg8, 1, 256);
   return kv8 ? v8 : v;
+}
+
+int align_tiles() {
+  static const int v = env_int("FD_ALIGN_TILES", kDefaultAlignTiles, 0, 4096);
+  return v;
 }
 
 // Programmatic dependent launch of the decode kernel (FD_PDL=0 turns it off):
@@ -544,6 +553,7 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
     p.timeout_ns = timeout_ns();
     p.epoch_word = reinterpret_cast<unsigned long long*>(ws + wl.epoch_off);
     p.num_blocks = num_blocks;
+    p.align_tiles = align_tiles();
     p.cost_tile = cost_tile();
     p.cost_seg = cost_seg();
     p.xworld = 0;
@@ -896,6 +906,7 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
     p.timeout_ns = timeout_ns();
     p.epoch_word = reinterpret_cast<unsigned long long*>(ws + wl.epoch_off);
     p.num_blocks = num_blocks;
+    p.align_tiles = align_tiles();
     p.cost_tile = cost_tile(true);
     p.cost_seg = cost_seg(true);
     p.xworld = 0;

@@ -535,6 +535,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   // loads, so the two round trips overlap.
   unsigned long long epoch_ld = 0;
   if (tid == 0) epoch_ld = *reinterpret_cast<volatile unsigned long long*>(p.epoch_word);
+  bool short_pairs = true;  // every sequence of this thread has at most p.align_tiles tiles
   for (int b = tid; b < batch; b += kSm100Threads) {
     const int stored = __ldg(p.seqlens + b);
     // keys cached before this step plus the ones it appended
@@ -543,6 +544,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     const int len = static_cast<int>(want > cap ? cap : want);
     lens[b] = len;
     prefix[b + 1] = cm.pair_cost(len);
+    short_pairs = short_pairs && seq_tiles(len) <= p.align_tiles;
   }
   if (tid == 0) {
     prefix[0] = 0;
@@ -550,13 +552,23 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   }
   fence_proxy_async_smem();
   tc_fence_before();
-  __syncthreads();
+  short_pairs = __syncthreads_and(short_pairs) != 0;
   tc_fence_after();
+  // Pair-aligned split: when there are no more (sequence, KV head) pairs
+  // than CTAs and every pair is short (<= align_tiles tiles), each CTA takes
+  // exactly one whole pair: no pair is cut, so no partial, arrival counter or
+  // merge lengthens a launch whose whole time is its latency chain.  Every
+  // pair then costs the same `aligned_cost` (more than its tiles' starts need:
+  // seg + (align_tiles - 1) full tiles), so range c of a grid of B * Hkv is
+  // exactly pair c.
+  const bool aligned = short_pairs && p.align_tiles > 0 &&
+                       static_cast<int64_t>(batch) * hkv <= static_cast<int64_t>(gridDim.x);
+  const int aligned_cost = cm.seg + p.align_tiles * cm.full() + 1;
   if (warp == 0) {  // inclusive scan of pair costs -> exclusive prefix sums
     int carry = 0;
     for (int base = 1; base <= batch; base += 32) {
       const int idx = base + lane;
-      int v = idx <= batch ? prefix[idx] : 0;
+      int v = idx <= batch ? (aligned ? aligned_cost : prefix[idx]) : 0;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int u = __shfl_up_sync(0xffffffffu, v, o);
@@ -583,7 +595,9 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   // every range holds at least one tile start: no CTA inside a pair's span is
   // empty, which the nseg count relies on.  CTAs past that (the host sized
   // the grid from an upper bound) have nothing to do.
-  {
+  if (aligned) {
+    sched.grid = batch * hkv;
+  } else {
     const int64_t g = sched.total / (cm.seg + cm.full() + 1);
     sched.grid = static_cast<int>(g < 1 ? 1 : (g < gridDim.x ? g : gridDim.x));
   }

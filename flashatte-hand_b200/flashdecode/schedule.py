@@ -27,6 +27,9 @@ DEFAULT_SEG = 12
 # in-kernel query split per pair): the kernel's defaults for that path
 E4M3_TILE_FIXED = 8
 E4M3_SEG = 48
+# pair-aligned split: one whole pair per CTA when B * Hkv <= grid and no
+# sequence has more than this many tiles
+DEFAULT_ALIGN_TILES = 16
 
 
 @dataclass(frozen=True)
@@ -60,15 +63,23 @@ def pair_cost(length: int, tile_fixed: int = DEFAULT_TILE_FIXED, seg: int = DEFA
 
 
 def segments(seqlens, hkv: int, grid: int, max_len: int | None = None,
-             tile_fixed: int = DEFAULT_TILE_FIXED, seg: int = DEFAULT_SEG) -> list[Segment]:
-    """All segments of all CTAs, in CTA order then work order (kernel's split)."""
+             tile_fixed: int = DEFAULT_TILE_FIXED, seg: int = DEFAULT_SEG,
+             align_tiles: int = 0) -> list[Segment]:
+    """All segments of all CTAs, in CTA order then work order (kernel's split).
+
+    align_tiles > 0: when B * Hkv <= grid and no sequence has more than
+    align_tiles tiles, every pair costs the same (seg + align_tiles full
+    tiles + 1) and the grid is B * Hkv, so CTA c takes exactly pair c."""
     lens = [min(max(0, int(L)), max_len) if max_len is not None else max(0, int(L)) for L in seqlens]
     full = FULL_TILE + tile_fixed
+    aligned = (align_tiles > 0 and len(lens) * hkv <= grid
+               and all(tiles_of(L) <= align_tiles for L in lens))
     prefix = [0]
     for L in lens:
-        prefix.append(prefix[-1] + pair_cost(L, tile_fixed, seg))
+        prefix.append(prefix[-1] + (seg + align_tiles * full + 1 if aligned
+                                    else pair_cost(L, tile_fixed, seg)))
     total = hkv * prefix[-1]
-    grid = max(1, min(grid, total // (seg + full + 1)))
+    grid = len(lens) * hkv if aligned else max(1, min(grid, total // (seg + full + 1)))
     npairs = len(lens) * hkv
 
     def range_start(c):

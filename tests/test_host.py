@@ -80,9 +80,11 @@ def test_lpt_partition_balances_skew(world):
     ([1, 127, 128, 129, 300, 0, 1000, 2049], 1, 148),
 ])
 @pytest.mark.parametrize("weights", ["16-bit", "e4m3"])
-def test_schedule_covers_every_tile_once(seqlens, hkv, grid, weights):
+@pytest.mark.parametrize("align", [0, schedule.DEFAULT_ALIGN_TILES, 64])
+def test_schedule_covers_every_tile_once(seqlens, hkv, grid, weights, align):
     kw = (dict(tile_fixed=schedule.E4M3_TILE_FIXED, seg=schedule.E4M3_SEG) if weights == "e4m3"
           else {})
+    kw["align_tiles"] = align
     segs = schedule.segments(seqlens, hkv, grid, **kw)
     seen = {}
     for s in segs:
@@ -104,6 +106,20 @@ def test_schedule_covers_every_tile_once(seqlens, hkv, grid, weights):
     for pair, ss in by_pair.items():
         assert len(ss) == ss[0].nseg
         assert [s.cta for s in ss] == list(range(ss[0].cfirst, ss[0].cfirst + ss[0].nseg))
+
+
+@pytest.mark.parametrize("seqlens,hkv", [([1, 2, 300, 0], 8), ([17] * 16, 4), ([141] * 16, 4),
+                                         ([512, 1, 7], 8)])
+def test_pair_aligned_split_takes_whole_pairs(seqlens, hkv):
+    """Few short pairs: one whole pair per CTA, nothing split or merged."""
+    segs = schedule.segments(seqlens, hkv, 148, align_tiles=schedule.DEFAULT_ALIGN_TILES)
+    assert [s.cta for s in segs] == list(range(len(seqlens) * hkv))
+    assert [s.pair for s in segs] == list(range(len(seqlens) * hkv))
+    assert all(s.nseg == 1 and s.tile0 == 0 and s.ntiles == schedule.tiles_of(seqlens[s.b])
+               for s in segs)
+    # a longer sequence, or more pairs than CTAs, goes back to the cost split
+    assert any(s.nseg > 1 for s in schedule.segments([5000] + seqlens, hkv, 148,
+                                                     align_tiles=schedule.DEFAULT_ALIGN_TILES))
 
 
 def _cta_costs(seqlens, hkv, grid):
@@ -170,3 +186,5 @@ def test_cost_defaults_match_the_host_library():
            for m in re.finditer(r"constexpr int (kDefaultCost\w+) = (\d+);", src)}
     assert got == {"kDefaultCostTile": schedule.DEFAULT_TILE_FIXED, "kDefaultCostSeg": schedule.DEFAULT_SEG,
                    "kDefaultCostTile8": schedule.E4M3_TILE_FIXED, "kDefaultCostSeg8": schedule.E4M3_SEG}
+    align = re.search(r"constexpr int kDefaultAlignTiles = (\d+);", src)
+    assert int(align.group(1)) == schedule.DEFAULT_ALIGN_TILES
