@@ -247,10 +247,21 @@ struct Schedule {
   const int* lens;         // [B] sequence lengths, clamped to [0, max_len] (smem)
   int64_t max_len, total;  // total = Hkv * cost_prefix[B]
   int batch, hkv, grid;
+  // Pair-aligned split (align_m > 0): every pair costs align_cost and CTA c
+  // takes the whole pairs [align_m * c, align_m * (c + 1)).
+  int align_m;
+  int64_t align_cost;
   CostModel cm;
 
   __device__ __forceinline__ int len_of(int b) const { return lens[b]; }
-  __device__ __forceinline__ int64_t range_start(int c) const { return total * c / grid; }
+  __device__ __forceinline__ int64_t range_start(int c) const {
+    if (align_m > 0) {
+      const int64_t pairs = static_cast<int64_t>(batch) * hkv;
+      const int64_t first_pair = static_cast<int64_t>(align_m) * c;
+      return align_cost * (first_pair < pairs ? first_pair : pairs);
+    }
+    return total * c / grid;
+  }
   // CTA whose range holds cost position s: largest c with range_start(c) <= s
   __device__ __forceinline__ int cta_of(int64_t s) const {
     return static_cast<int>(((s + 1) * grid + total - 1) / total - 1);
@@ -535,7 +546,12 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   // loads, so the two round trips overlap.
   unsigned long long epoch_ld = 0;
   if (tid == 0) epoch_ld = *reinterpret_cast<volatile unsigned long long*>(p.epoch_word);
-  bool short_pairs = true;  // every sequence of this thread has at most p.align_tiles tiles
+  // Pair-aligned split (below): whole pairs per CTA when every sequence has
+  // at most align_tiles / m tiles, m = pairs per CTA = ceil(B * Hkv / grid).
+  const int64_t n_pairs = static_cast<int64_t>(batch) * hkv;
+  const int align_m = static_cast<int>((n_pairs + gridDim.x - 1) / gridDim.x);
+  const int align_max_tiles = p.align_tiles / align_m;
+  bool short_pairs = true;  // every sequence of this thread has at most align_max_tiles tiles
   for (int b = tid; b < batch; b += kSm100Threads) {
     const int stored = __ldg(p.seqlens + b);
     // keys cached before this step plus the ones it appended
@@ -544,7 +560,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     const int len = static_cast<int>(want > cap ? cap : want);
     lens[b] = len;
     prefix[b + 1] = cm.pair_cost(len);
-    short_pairs = short_pairs && seq_tiles(len) <= p.align_tiles;
+    short_pairs = short_pairs && seq_tiles(len) <= align_max_tiles;
   }
   if (tid == 0) {
     prefix[0] = 0;
@@ -554,15 +570,14 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   tc_fence_before();
   short_pairs = __syncthreads_and(short_pairs) != 0;
   tc_fence_after();
-  // Pair-aligned split: when there are no more (sequence, KV head) pairs
-  // than CTAs and every pair is short (<= align_tiles tiles), each CTA takes
-  // exactly one whole pair: no pair is cut, so no partial, arrival counter or
-  // merge lengthens a launch whose whole time is its latency chain.  Every
-  // pair then costs the same `aligned_cost` (more than its tiles' starts need:
-  // seg + (align_tiles - 1) full tiles), so range c of a grid of B * Hkv is
-  // exactly pair c.
-  const bool aligned = short_pairs && p.align_tiles > 0 &&
-                       static_cast<int64_t>(batch) * hkv <= static_cast<int64_t>(gridDim.x);
+  // Pair-aligned split: when every CTA's share is short — m = ceil(B * Hkv /
+  // grid) whole pairs of at most align_tiles / m tiles each, so at most
+  // align_tiles tiles per CTA — each CTA takes m whole pairs: no pair is
+  // cut, so no partial, arrival counter or merge lengthens a launch whose
+  // whole time is its latency chain.  Every pair then costs the same
+  // `aligned_cost` (more than its tiles' starts need: seg + (align_tiles - 1)
+  // full tiles) and range c is exactly pairs [m c, m (c + 1)).
+  const bool aligned = short_pairs && align_max_tiles > 0;
   const int aligned_cost = cm.seg + p.align_tiles * cm.full() + 1;
   if (warp == 0) {  // inclusive scan of pair costs -> exclusive prefix sums
     int carry = 0;
@@ -595,8 +610,10 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   // every range holds at least one tile start: no CTA inside a pair's span is
   // empty, which the nseg count relies on.  CTAs past that (the host sized
   // the grid from an upper bound) have nothing to do.
+  sched.align_m = aligned ? align_m : 0;
+  sched.align_cost = aligned_cost;
   if (aligned) {
-    sched.grid = batch * hkv;
+    sched.grid = static_cast<int>((n_pairs + align_m - 1) / align_m);
   } else {
     const int64_t g = sched.total / (cm.seg + cm.full() + 1);
     sched.grid = static_cast<int>(g < 1 ? 1 : (g < gridDim.x ? g : gridDim.x));

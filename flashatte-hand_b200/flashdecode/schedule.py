@@ -67,22 +67,25 @@ def segments(seqlens, hkv: int, grid: int, max_len: int | None = None,
              align_tiles: int = 0) -> list[Segment]:
     """All segments of all CTAs, in CTA order then work order (kernel's split).
 
-    align_tiles > 0: when B * Hkv <= grid and no sequence has more than
-    align_tiles tiles, every pair costs the same (seg + align_tiles full
-    tiles + 1) and the grid is B * Hkv, so CTA c takes exactly pair c."""
+    align_tiles > 0: with m = ceil(B * Hkv / grid) pairs per CTA, when no
+    sequence has more than align_tiles // m tiles, every pair costs the same
+    (seg + align_tiles full tiles + 1) and CTA c takes exactly the whole
+    pairs [m c, m (c + 1))."""
     lens = [min(max(0, int(L)), max_len) if max_len is not None else max(0, int(L)) for L in seqlens]
     full = FULL_TILE + tile_fixed
-    aligned = (align_tiles > 0 and len(lens) * hkv <= grid
-               and all(tiles_of(L) <= align_tiles for L in lens))
+    npairs = len(lens) * hkv
+    m = -(-npairs // grid)
+    aligned = align_tiles // m > 0 and all(tiles_of(L) <= align_tiles // m for L in lens)
+    k_aligned = seg + align_tiles * full + 1
     prefix = [0]
     for L in lens:
-        prefix.append(prefix[-1] + (seg + align_tiles * full + 1 if aligned
-                                    else pair_cost(L, tile_fixed, seg)))
+        prefix.append(prefix[-1] + (k_aligned if aligned else pair_cost(L, tile_fixed, seg)))
     total = hkv * prefix[-1]
-    grid = len(lens) * hkv if aligned else max(1, min(grid, total // (seg + full + 1)))
-    npairs = len(lens) * hkv
+    grid = -(-npairs // m) if aligned else max(1, min(grid, total // (seg + full + 1)))
 
     def range_start(c):
+        if aligned:
+            return k_aligned * min(m * c, npairs)
         return total * c // grid
 
     def cta_of(s):

@@ -117,9 +117,22 @@ def test_pair_aligned_split_takes_whole_pairs(seqlens, hkv):
     assert [s.pair for s in segs] == list(range(len(seqlens) * hkv))
     assert all(s.nseg == 1 and s.tile0 == 0 and s.ntiles == schedule.tiles_of(seqlens[s.b])
                for s in segs)
-    # a longer sequence, or more pairs than CTAs, goes back to the cost split
+    # a longer sequence goes back to the cost split
     assert any(s.nseg > 1 for s in schedule.segments([5000] + seqlens, hkv, 148,
                                                      align_tiles=schedule.DEFAULT_ALIGN_TILES))
+
+
+@pytest.mark.parametrize("seqlens,hkv,m", [([8] * 64, 4, 2), ([362] * 32, 8, 2), ([100] * 300, 4, 9)])
+def test_pair_aligned_split_several_pairs_per_cta(seqlens, hkv, m):
+    """More pairs than CTAs: m = ceil(pairs / 148) whole pairs per CTA while
+    m pairs stay within the tile budget; otherwise the cost split."""
+    segs = schedule.segments(seqlens, hkv, 148, align_tiles=schedule.DEFAULT_ALIGN_TILES)
+    per_cta_tiles = m * schedule.tiles_of(seqlens[0])
+    if per_cta_tiles <= schedule.DEFAULT_ALIGN_TILES:
+        assert all(s.nseg == 1 and s.cta == s.pair // m for s in segs)
+        assert max(s.cta for s in segs) + 1 == -(-len(seqlens) * hkv // m)
+    else:
+        assert any(s.nseg > 1 for s in segs)
 
 
 def _cta_costs(seqlens, hkv, grid):
