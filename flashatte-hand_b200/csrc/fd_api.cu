@@ -182,7 +182,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 int esize(int dtype) { return dtype == FD_DTYPE_FP32 ? 4 : 2; }
 
 // Tuning knobs (FD_TMA_CHUNK, FD_COST_TILE / FD_COST_SEG and their e4m3
-// twins, FD_PDL, FD_WAIT_TIMEOUT_NS) are read from the environment only when
+// twins, FD_ALIGN_TILES, FD_PDL, FD_WAIT_TIMEOUT_NS) are read from the
+// environment only when
 // FD_DEBUG_KNOBS=1: without that switch a caller's environment cannot change
 // the schedule or the timeouts of the operator.
 const char* knob(const char* name) {
