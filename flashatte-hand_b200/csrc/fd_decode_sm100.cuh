@@ -263,6 +263,7 @@ struct Schedule {
     return total * c / grid;
   }
   // CTA whose range holds cost position s: largest c with range_start(c) <= s
+  // (cost split only: the pair-aligned split cuts no pair, so it never asks)
   __device__ __forceinline__ int cta_of(int64_t s) const {
     return static_cast<int>(((s + 1) * grid + total - 1) / total - 1);
   }

@@ -283,7 +283,7 @@ int fd_combine_lse(const float* part_o, int64_t part_o_stride, const float* part
  * fd_xgpu_open.  fd_decode_paged_xgpu then runs one step: the decode kernel
  * writes this rank's partial (O, LSE) for every output row straight into
  * every rank's buffer over NVLink and flags it; a merge kernel waits (bounded,
- * FD_ERR_DEVICE_TIMEOUT in the workspace error word on expiry) for all ranks'
+ * FD_ERR_DEVICE_TIMEOUT in the device status word on expiry) for all ranks'
  * flags and writes out [B, sq, Hq, D] and lse [B, Hq, sq] on every rank.
  * xbufs: host array of `world` device pointers, entry rank = own buffer.
  * step: call counter, the same on every rank, +1 per call (the buffer is
