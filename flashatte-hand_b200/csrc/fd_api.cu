@@ -43,6 +43,8 @@ constexpr int kDefaultCostSeg8 = 48;
 // launches with no more pairs than SMs and no sequence longer than this
 // many 128-token tiles (see the schedule set-up in fd_decode_sm100.cuh).
 constexpr int kDefaultAlignTiles = 16;
+// Short launches on the CUDA-core kernel (see simt_max_tokens).
+constexpr int kDefaultSimtMaxTokens = 64;
 
 thread_local int t_last_error = FD_OK;
 thread_local char t_last_msg[256] = "ok";
@@ -182,7 +184,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 int esize(int dtype) { return dtype == FD_DTYPE_FP32 ? 4 : 2; }
 
 // Tuning knobs (FD_TMA_CHUNK, FD_COST_TILE / FD_COST_SEG and their e4m3
-// twins, FD_ALIGN_TILES, FD_PDL, FD_WAIT_TIMEOUT_NS) are read from the
+// twins, FD_ALIGN_TILES, FD_SIMT_MAX_TOKENS, FD_PDL, FD_WAIT_TIMEOUT_NS) are read from the
 // environment only when
 // FD_DEBUG_KNOBS=1: without that switch a caller's environment cannot change
 // the schedule or the timeouts of the operator.
@@ -297,6 +299,16 @@ int align_tiles() {
   return v;
 }
 
+// Launches whose sequences are all at most this many tokens long (bounded by
+// the block table's width times the page, or by max_seqlen_k when given) run
+// on the CUDA-core kernel: its one CTA per query head has a shorter latency
+// chain than the tensor-core pipeline's fill, and the few kilobytes of K/V
+// such a launch reads stay in L2 (FD_SIMT_MAX_TOKENS).
+int simt_max_tokens() {
+  static const int v = env_int("FD_SIMT_MAX_TOKENS", kDefaultSimtMaxTokens, 0, 1 << 20);
+  return v;
+}
+
 // Programmatic dependent launch of the decode kernel (FD_PDL=0 turns it off):
 // its prologue may overlap the previous kernel on the stream; it reads no
 // input before that kernel has completed.
@@ -324,6 +336,13 @@ int* device_status_word() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
   return status_word(dev);
+}
+
+bool is_short_launch(int64_t block_table_stride, int64_t page_block_size, int64_t max_seqlen_k) {
+  const int64_t table_tokens = block_table_stride * page_block_size;
+  const int64_t bound =
+      max_seqlen_k > 0 && max_seqlen_k < table_tokens ? max_seqlen_k : table_tokens;
+  return bound <= simt_max_tokens();
 }
 
 bool uses_tensor_core_path(const void* q, const void* k_cache, const void* v_cache,
@@ -442,7 +461,10 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
   const int chunk = pick_chunk(page_block_size);
   const int64_t qrows = seqlen_q * group;
 
+  const bool short_launch =
+      xa == nullptr && fd::is_short_launch(block_table_stride, page_block_size, max_seqlen_k);
   const bool tensor_core_path =
+      !short_launch &&
       fd::uses_tensor_core_path(q, k_cache, v_cache, headdim, qrows, page_block_size);
   if (xa != nullptr && (!tensor_core_path || batch_size > fd::kMaxBatchPerLaunch))
     return set_error(FD_ERR_UNSUPPORTED,

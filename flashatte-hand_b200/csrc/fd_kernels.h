@@ -157,6 +157,12 @@ constexpr int kStatusBadPage = 6;
 // library, looked up once per device); nullptr if the lookup failed.
 int* device_status_word();
 
+// Whether a 16-bit decode is short enough (every sequence at most
+// FD_SIMT_MAX_TOKENS long, bounded by the block table's width times the
+// page or by max_seqlen_k when given) to run on the CUDA-core kernel, whose
+// latency chain is shorter than the tensor-core pipeline's fill.
+bool is_short_launch(int64_t block_table_stride, int64_t page_block_size, int64_t max_seqlen_k);
+
 // Whether a 16-bit decode of this shape runs on the tensor-core kernel (and so
 // uses split scratch) rather than the CUDA-core kernel, which needs none.
 bool uses_tensor_core_path(const void* q, const void* k_cache, const void* v_cache,

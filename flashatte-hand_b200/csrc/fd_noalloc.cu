@@ -63,11 +63,13 @@ extern "C" int fd_decode_paged_noalloc(const void* q, const void* k_cache, const
   if (scratch == nullptr)
     return fd::report_error(FD_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s",
                             cudaGetErrorString(status));
-  // Shapes the CUDA-core kernel takes use no split scratch at all: they are
-  // never refused for its size.  (Invalid arguments are left to
+  // Shapes the CUDA-core kernel takes (other head dims, wide groups,
+  // unaligned pointers, short launches) use no split scratch at all: they
+  // are never refused for its size.  (Invalid arguments are left to
   // fd_decode_paged to report.)
   const bool uses_scratch =
       num_heads > 0 && num_heads_k > 0 && num_heads % num_heads_k == 0 &&
+      !fd::is_short_launch(block_table_stride, page_block_size, max_seqlen_k) &&
       fd::uses_tensor_core_path(q, k_cache, v_cache, headdim, num_heads / num_heads_k,
                                 page_block_size);
   if (uses_scratch) {

@@ -139,7 +139,8 @@ def test_noalloc_refuses_shapes_beyond_its_scratch(lib):
     assert need > NOALLOC_SCRATCH_BYTES
     buf = torch.zeros(4096, dtype=torch.int32, device="cuda")
     p = buf.data_ptr()
-    status = lib.fd_decode_paged_noalloc(p, p, p, p, None, p, p, 1, B, Hq, Hkv, 128, 16, 1, 0, 0,
+    # a 64-page table row (1024 tokens): long enough for the tensor-core kernel
+    status = lib.fd_decode_paged_noalloc(p, p, p, p, None, p, p, 64, B, Hq, Hkv, 128, 16, 1, 0, 0,
                                          ctypes.c_float(0.1), 0, None)
     assert status == 3
     assert "scratch" in flashdecode.last_error()[1]
