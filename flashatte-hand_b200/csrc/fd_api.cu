@@ -181,6 +181,19 @@ void* internal_workspace(int dev, size_t bytes, cudaStream_t stream, const char*
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Sequences per launch.  The kernel keeps per-sequence cost prefix sums in
+// int32 and divides cost positions in 32 bits, so a launch's cost line (per
+// sequence at most per_seq_cost, or the pair-aligned split's per-pair cost,
+// times Hkv) times (grid + 1) must stay below 2^32.  0: not even one fits.
+int64_t seqs_per_launch(int64_t per_seq_cost, int64_t aligned_cost, int64_t hkv, int sms) {
+  const int64_t c = per_seq_cost > aligned_cost ? per_seq_cost : aligned_cost;
+  const int64_t line = c * hkv * (static_cast<int64_t>(sms) + 1);
+  if (c > INT32_MAX || line > static_cast<int64_t>(UINT32_MAX)) return 0;
+  int64_t n = static_cast<int64_t>(UINT32_MAX) / line;
+  if (n > INT32_MAX / c) n = INT32_MAX / c;
+  return n < fd::kMaxBatchPerLaunch ? n : fd::kMaxBatchPerLaunch;
+}
+
 int esize(int dtype) { return dtype == FD_DTYPE_FP32 ? 4 : 2; }
 
 // Tuning knobs (FD_TMA_CHUNK, FD_COST_TILE / FD_COST_SEG and their e4m3
@@ -518,14 +531,16 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
     if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "K/V tensor map encode failed (%d)", (int)r);
   }
 
-  // The kernel keeps per-sequence cost prefix sums in int32: bound the batch
-  // of one launch so the sum cannot overflow.
+  // Bound the batch of one launch so the kernel's cost arithmetic fits.
   const int64_t per_seq_cost =
       cost_seg() + ((kv_max + fd::kTileTokens - 1) / fd::kTileTokens + 1) *
                        (8 + static_cast<int64_t>(cost_tile()));
-  if (per_seq_cost > INT32_MAX) return set_error(FD_ERR_UNSUPPORTED, "sequence too long");
-  int64_t per_launch = INT32_MAX / per_seq_cost;
-  if (per_launch > fd::kMaxBatchPerLaunch) per_launch = fd::kMaxBatchPerLaunch;
+  const int64_t per_launch = seqs_per_launch(
+      per_seq_cost, cost_seg() + static_cast<int64_t>(align_tiles()) * (8 + cost_tile()) + 1,
+      num_heads_k, sms);
+  if (per_launch == 0) return set_error(FD_ERR_UNSUPPORTED, "sequence too long");
+  if (xa != nullptr && per_launch < batch_size)
+    return set_error(FD_ERR_UNSUPPORTED, "cross-GPU exchange: the batch does not fit one launch");
   for (int64_t b0 = 0; b0 < batch_size; b0 += per_launch) {
     const int64_t nb = batch_size - b0 < per_launch ? batch_size - b0 : per_launch;
     {
@@ -898,9 +913,13 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
   const int64_t per_seq_cost =
       cost_seg(true) + ((kv_max + fd::kTileTokens - 1) / fd::kTileTokens + 1) *
                        (8 + static_cast<int64_t>(cost_tile(true)));
-  if (per_seq_cost > INT32_MAX) return set_error(FD_ERR_UNSUPPORTED, "sequence too long");
-  int64_t per_launch = INT32_MAX / per_seq_cost;
-  if (per_launch > fd::kMaxBatchPerLaunch) per_launch = fd::kMaxBatchPerLaunch;
+  const int64_t per_launch = seqs_per_launch(
+      per_seq_cost,
+      cost_seg(true) + static_cast<int64_t>(align_tiles()) * (8 + cost_tile(true)) + 1,
+      num_heads_k, sms);
+  if (per_launch == 0) return set_error(FD_ERR_UNSUPPORTED, "sequence too long");
+  if (xa != nullptr && per_launch < batch_size)
+    return set_error(FD_ERR_UNSUPPORTED, "cross-GPU exchange: the batch does not fit one launch");
   const int es = esize(q_dtype);
   std::memset(&maps.q, 0, sizeof(maps.q));  // the e4m3 kernel reads the query through p.q
   for (int64_t b0 = 0; b0 < batch_size; b0 += per_launch) {

@@ -232,7 +232,15 @@ __device__ __forceinline__ int seq_tiles(int len) {
   return len > 0 ? (len + kTileTokens - 1) / kTileTokens : 1;
 }
 
-__device__ __forceinline__ int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+// Divisions of the schedule, in 32 bits: the host caps a launch's batch so
+// that its cost line times (grid + 1) stays below 2^32 (all the schedule's
+// cost positions, and a position times the grid, fit in 32 bits).  A 64-bit
+// integer division is a long software sequence, and these run, cold, on
+// every CTA's path to its first load.
+__device__ __forceinline__ int64_t div_u32(int64_t a, int64_t b) {
+  return static_cast<int64_t>(static_cast<uint32_t>(a) / static_cast<uint32_t>(b));
+}
+__device__ __forceinline__ int64_t ceil_div_u32(int64_t a, int64_t b) { return div_u32(a + b - 1, b); }
 
 // One segment of a CTA's work: tiles tile0 .. tile0+ntiles-1 of pair (b, kvh).
 struct Segment {
@@ -260,12 +268,12 @@ struct Schedule {
       const int64_t first_pair = static_cast<int64_t>(align_m) * c;
       return align_cost * (first_pair < pairs ? first_pair : pairs);
     }
-    return total * c / grid;
+    return div_u32(total * c, grid);
   }
   // CTA whose range holds cost position s: largest c with range_start(c) <= s
   // (cost split only: the pair-aligned split cuts no pair, so it never asks)
   __device__ __forceinline__ int cta_of(int64_t s) const {
-    return static_cast<int>(((s + 1) * grid + total - 1) / total - 1);
+    return static_cast<int>(div_u32((s + 1) * grid + total - 1, total) - 1);
   }
   __device__ __forceinline__ int64_t pair_start(int pair) const {
     const int b = pair / hkv, kvh = pair - b * hkv;
@@ -317,14 +325,14 @@ struct Schedule {
       if (static_cast<int64_t>(hkv) * cost_prefix[mid] <= e0) lo = mid; else hi = mid - 1;
     }
     const int pc = cost_prefix[lo + 1] - cost_prefix[lo];
-    int kvh = static_cast<int>((e0 - static_cast<int64_t>(hkv) * cost_prefix[lo]) / pc);
+    int kvh = static_cast<int>(div_u32(e0 - static_cast<int64_t>(hkv) * cost_prefix[lo], pc));
     kvh = kvh < hkv - 1 ? kvh : hkv - 1;
     const int pair = lo * hkv + kvh;
     const int64_t cp = pair_start(pair);
     int j0 = 0;
     if (e0 > cp) {
       const int64_t x = e0 - cp - cm.seg;
-      j0 = static_cast<int>(x > 0 ? ceil_div64(x, cm.full()) : 1);
+      j0 = static_cast<int>(x > 0 ? ceil_div_u32(x, cm.full()) : 1);
       if (j0 < 1) j0 = 1;
     }
     if (make(pair, j0, e1, s)) return true;
@@ -550,7 +558,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   // Pair-aligned split (below): whole pairs per CTA when every sequence has
   // at most align_tiles / m tiles, m = pairs per CTA = ceil(B * Hkv / grid).
   const int64_t n_pairs = static_cast<int64_t>(batch) * hkv;
-  const int align_m = static_cast<int>((n_pairs + gridDim.x - 1) / gridDim.x);
+  const int align_m = static_cast<int>(ceil_div_u32(n_pairs, gridDim.x));
   const int align_max_tiles = p.align_tiles / align_m;
   bool short_pairs = true;  // every sequence of this thread has at most align_max_tiles tiles
   for (int b = tid; b < batch; b += kSm100Threads) {
@@ -614,9 +622,9 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   sched.align_m = aligned ? align_m : 0;
   sched.align_cost = aligned_cost;
   if (aligned) {
-    sched.grid = static_cast<int>((n_pairs + align_m - 1) / align_m);
+    sched.grid = static_cast<int>(ceil_div_u32(n_pairs, align_m));
   } else {
-    const int64_t g = sched.total / (cm.seg + cm.full() + 1);
+    const int64_t g = div_u32(sched.total, cm.seg + cm.full() + 1);
     sched.grid = static_cast<int>(g < 1 ? 1 : (g < gridDim.x ? g : gridDim.x));
   }
   const int64_t range_end = sched.range_start(cta + 1);
