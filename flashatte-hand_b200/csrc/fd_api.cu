@@ -26,6 +26,7 @@
 
 #include "../../include/flashdecode.h"
 #include "fd_kernels.h"
+#include "fd_trace.h"
 
 namespace {
 
@@ -434,6 +435,7 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
                 int dtype, int out_dtype, float softmax_scale, int causal, int64_t max_seqlen_k,
                 int len_add, void* workspace, size_t workspace_bytes, void* stream,
                 const ExchangeArgs* xa, int** err_word) {
+  fd::TraceRange trace("decode");
   if (xa != nullptr) out = xa->part[0];  // results go to the exchange parts
   if (q == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr ||
       cache_seqlens == nullptr || block_table == nullptr)
@@ -626,6 +628,7 @@ template <typename Decode>
 int xgpu_step(int64_t batch_size, int64_t seqlen_q, int64_t num_heads, int rank, int world,
               void* const* xbufs, uint64_t step, void* out, int out_dtype, float* lse,
               void* stream, Decode&& decode) {
+  fd::TraceRange trace("exchange");
   if (xbufs == nullptr || out == nullptr) return set_error(FD_ERR_INVALID_ARG, "null pointer");
   if (world < 1 || world > fd::kMaxExchangeRanks || rank < 0 || rank >= world)
     return set_error(FD_ERR_INVALID_ARG, "rank %d / world %d", rank, world);
@@ -751,6 +754,7 @@ int fd_append_kv_paged(const void* k_new, const void* v_new, void* k_cache, void
                        int64_t block_table_stride, int64_t batch_size, int64_t seqlen_new,
                        int64_t num_heads_k, int64_t headdim, int64_t page_block_size,
                        int64_t num_blocks, int dtype, void* stream) {
+  fd::TraceRange trace("append");
   if (k_new == nullptr || v_new == nullptr || k_cache == nullptr || v_cache == nullptr ||
       cache_seqlens == nullptr || block_table == nullptr)
     return set_error(FD_ERR_INVALID_ARG, "null tensor pointer");
@@ -873,6 +877,7 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
                            int causal, int64_t max_seqlen_k, int len_add, void* workspace,
                            size_t workspace_bytes, void* stream,
                            const ExchangeArgs* xa = nullptr, int** err_word = nullptr) {
+  fd::TraceRange trace("decode_e4m3");
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return set_error(FD_ERR_CUDA, "no current CUDA device");
@@ -1022,6 +1027,7 @@ int fd_append_kv_paged_fp8(const void* k_new, const void* v_new, void* k_cache, 
                            int64_t block_table_stride, int64_t batch_size, int64_t seqlen_new,
                            int64_t num_heads_k, int64_t headdim, int64_t page_block_size,
                            int64_t num_blocks, int src_dtype, void* stream) {
+  fd::TraceRange trace("append_e4m3");
   if (k_new == nullptr || v_new == nullptr || k_cache == nullptr || v_cache == nullptr ||
       k_scale == nullptr || v_scale == nullptr || cache_seqlens == nullptr || block_table == nullptr)
     return set_error(FD_ERR_INVALID_ARG, "null pointer");
@@ -1130,6 +1136,7 @@ void run_kernel(const void* q, const void* k_cache_paged, const void* v_cache_pa
 int fd_combine_lse(const float* part_o, int64_t part_o_stride, const float* part_lse,
                    int64_t part_lse_stride, int64_t n_parts, int64_t rows, int64_t headdim,
                    void* out, int out_dtype, float* lse_out, void* stream) {
+  fd::TraceRange trace("combine_lse");
   if (part_o == nullptr || part_lse == nullptr || out == nullptr)
     return set_error(FD_ERR_INVALID_ARG, "null pointer");
   if (n_parts <= 0 || rows < 0 || headdim <= 0 || rows > INT32_MAX)
