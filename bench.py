@@ -511,13 +511,20 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
         clk.mark("begin")
+        # Events after each of the first few timed calls as well: a short
+        # window opens on an idle GPU, and the first call carries the host
+        # issue the later ones overlap (reported as first_calls_us).
+        first_evs = [torch.cuda.Event(enable_timing=True) for _ in range(min(args.steps, 5))]
         ev0.record(stream)
-        for _ in range(args.steps):
+        for i in range(args.steps):
             step()
+            if i < len(first_evs):
+                first_evs[i].record(stream)
         ev1.record(stream)
         torch.cuda.synchronize()
         clk.mark("end")
     ms = ev0.elapsed_time(ev1)
+    first_calls_us = [round(a.elapsed_time(b) * 1e3, 1) for a, b in zip([ev0] + first_evs, first_evs)]
     if dist is not None:
         dist.barrier()
         tt = torch.tensor([ms], device="cuda")
@@ -651,6 +658,7 @@ def main():
         "data": "synthetic", "config": config,
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": launches_per_call * args.steps, "clocks": clk.summary(),
+        "first_calls_us": first_calls_us,
     }
     if xgpu_check is not None:
         line["xgpu_check"] = xgpu_check
