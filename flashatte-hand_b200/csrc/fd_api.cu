@@ -40,6 +40,16 @@ constexpr int kDefaultCostSeg = 12;
 // short sequences overloaded (295 us); these give 198 us.
 constexpr int kDefaultCostTile8 = 8;
 constexpr int kDefaultCostSeg8 = 48;
+// Least cost of a pair (see CostModel in fd_decode_sm100.cuh): a pair of a
+// tile or two is a latency chain (query load, QK, softmax, PV, finish) that
+// the ring cannot hide behind streaming, so its share of a CTA's range is
+// raised to 40 units (four full tiles).  Measured on one B200 against no
+// floor: config 3's 8-way batch shard 65.4 -> 54.4 us, its 4-way shard
+// 97.1 -> 90.9 us, contest B=64 L=2048 41.6 -> 37.3 us and B=32 L=4096
+// 59.2 -> 54.2 us; pairs of four tiles or more (config 5, config 2) keep
+// their cost and their times.  A larger seg for every pair gains about as
+// much on config 3 but slows the page-16 config 5 mixes.
+constexpr int kDefaultCostFloor = 40;
 // Pair-aligned split (one whole (sequence, KV head) pair per CTA) for
 // launches with no more pairs than SMs and no sequence longer than this
 // many 128-token tiles (see the schedule set-up in fd_decode_sm100.cuh).
@@ -197,8 +207,8 @@ int64_t seqs_per_launch(int64_t per_seq_cost, int64_t aligned_cost, int64_t hkv,
 
 int esize(int dtype) { return dtype == FD_DTYPE_FP32 ? 4 : 2; }
 
-// Tuning knobs (FD_TMA_CHUNK, FD_COST_TILE / FD_COST_SEG and their e4m3
-// twins, FD_ALIGN_TILES, FD_SIMT_MAX_TOKENS, FD_PDL, FD_WAIT_TIMEOUT_NS) are read from the
+// Tuning knobs (FD_TMA_CHUNK, FD_COST_TILE / FD_COST_SEG / FD_COST_FLOOR and
+// the e4m3 twins of the first two, FD_ALIGN_TILES, FD_SIMT_MAX_TOKENS, FD_PDL, FD_WAIT_TIMEOUT_NS) are read from the
 // environment only when
 // FD_DEBUG_KNOBS=1: without that switch a caller's environment cannot change
 // the schedule or the timeouts of the operator.
@@ -306,6 +316,17 @@ int cost_seg(bool kv8 = false) {
   static const int v = env_int("FD_COST_SEG", kDefaultCostSeg, 1, 256);
   static const int v8 = env_int("FD_COST_SEG8", kDefaultCostSeg8, 1, 256);
   return kv8 ? v8 : v;
+}
+
+// 16-bit caches only (e4m3 launches use no floor).
+int cost_floor() {
+  static const int v = env_int("FD_COST_FLOOR", kDefaultCostFloor, 0, 1024);
+  return v;
+}
+// Largest per-pair part (`lead`) of any pair under the cost model.
+int64_t max_lead(bool kv8 = false) {
+  const int floor = kv8 ? 0 : cost_floor();
+  return cost_seg(kv8) > floor ? cost_seg(kv8) : floor;
 }
 
 int align_tiles() {
@@ -535,10 +556,10 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
 
   // Bound the batch of one launch so the kernel's cost arithmetic fits.
   const int64_t per_seq_cost =
-      cost_seg() + ((kv_max + fd::kTileTokens - 1) / fd::kTileTokens + 1) *
+      max_lead() + ((kv_max + fd::kTileTokens - 1) / fd::kTileTokens + 1) *
                        (8 + static_cast<int64_t>(cost_tile()));
   const int64_t per_launch = seqs_per_launch(
-      per_seq_cost, cost_seg() + static_cast<int64_t>(align_tiles()) * (8 + cost_tile()) + 1,
+      per_seq_cost, max_lead() + static_cast<int64_t>(align_tiles()) * (8 + cost_tile()) + 1,
       num_heads_k, sms);
   if (per_launch == 0) return set_error(FD_ERR_UNSUPPORTED, "sequence too long");
   if (xa != nullptr && per_launch < batch_size)
@@ -596,6 +617,7 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, void* o
     p.align_tiles = align_tiles();
     p.cost_tile = cost_tile();
     p.cost_seg = cost_seg();
+    p.cost_floor = cost_floor();
     p.xworld = 0;
     p.pdl = (xa == nullptr && pdl_enabled()) ? 1 : 0;
     p.len_add = len_add;
@@ -956,6 +978,7 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
     p.align_tiles = align_tiles();
     p.cost_tile = cost_tile(true);
     p.cost_seg = cost_seg(true);
+    p.cost_floor = 0;
     p.xworld = 0;
     p.pdl = (xa == nullptr && pdl_enabled()) ? 1 : 0;
     p.len_add = len_add;

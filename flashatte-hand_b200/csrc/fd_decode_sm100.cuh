@@ -212,20 +212,31 @@ template <> __device__ __forceinline__ __half to_out<__half>(float x) { return _
 // 128-token tile cost kFullTile = 8, a tile also costs `tile_fixed` (its
 // fixed QK / softmax / PV work), a sequence's partial last tile costs its
 // 16-token boxes instead of 8, and every (sequence, KV head) pair costs
-// `seg` once (its set-up and epilogue).  Pairs are laid end to end
-// (b-major, then KV head); CTA c takes the tiles whose start cost lies in
-// [C*c/G, C*(c+1)/G).  Every tile belongs to exactly one CTA; a pair
-// spread over several CTAs is merged by the last of them.
+// `seg` once (its set-up and epilogue), raised where needed so that no pair
+// costs less than `floor` (a pair of a few tiles is a latency chain that
+// the ring cannot hide behind streaming).  This per-pair part is the pair's
+// `lead`: its first tile starts at the pair's start and tile j >= 1 at
+// start + lead + j * full.  Pairs are laid end to end (b-major, then KV
+// head); CTA c takes the tiles whose start cost lies in [C*c/G, C*(c+1)/G).
+// Every tile belongs to exactly one CTA; a pair spread over several CTAs is
+// merged by the last of them.
 constexpr int kFullTile = 8;
 
 struct CostModel {
-  int tile_fixed, seg;
+  int tile_fixed, seg, floor;
   __device__ __forceinline__ int full() const { return kFullTile + tile_fixed; }
-  // cost of one pair of a sequence of `len` tokens
-  __device__ __forceinline__ int pair_cost(int len) const {
+  // cost of the tiles of one pair of a sequence of `len` tokens
+  __device__ __forceinline__ int tiles_cost(int len) const {
     const int n_full = len / kTileTokens, rem = len % kTileTokens;
-    return seg + n_full * full() + ((rem > 0 || len == 0) ? (rem + 15) / 16 + tile_fixed : 0);
+    return n_full * full() + ((rem > 0 || len == 0) ? (rem + 15) / 16 + tile_fixed : 0);
   }
+  __device__ __forceinline__ int lead(int len) const {
+    const int raised = floor - tiles_cost(len);
+    return raised > seg ? raised : seg;
+  }
+  __device__ __forceinline__ int pair_cost(int len) const { return lead(len) + tiles_cost(len); }
+  // upper bound of any pair's lead
+  __device__ __forceinline__ int max_lead() const { return floor > seg ? floor : seg; }
 };
 
 __device__ __forceinline__ int seq_tiles(int len) {
@@ -280,8 +291,9 @@ struct Schedule {
     return static_cast<int64_t>(hkv) * cost_prefix[b] +
            static_cast<int64_t>(kvh) * (cost_prefix[b + 1] - cost_prefix[b]);
   }
-  __device__ __forceinline__ int64_t tile_start(int64_t cp, int j) const {
-    return j == 0 ? cp : cp + cm.seg + static_cast<int64_t>(j) * cm.full();
+  // start of tile j of the pair that starts at cp and has lead `lead`
+  __device__ __forceinline__ int64_t tile_start(int64_t cp, int lead, int j) const {
+    return j == 0 ? cp : cp + lead + static_cast<int64_t>(j) * cm.full();
   }
   // Segment of `pair` from tile j0 on, cut at range end e1; false if no tile
   // of the pair at or after j0 starts before e1.  Integer work here is 32-bit
@@ -290,10 +302,11 @@ struct Schedule {
     const int b = pair / hkv;
     const int len = len_of(b);
     const int n = seq_tiles(len);
+    const int lead = cm.lead(len);
     const int64_t cp = pair_start(pair);
-    if (j0 >= n || tile_start(cp, j0) >= e1) return false;
-    // last tile with start < e1: j <= ceil((e1 - cp - seg) / full) - 1
-    const int64_t x64 = e1 - cp - cm.seg;
+    if (j0 >= n || tile_start(cp, lead, j0) >= e1) return false;
+    // last tile with start < e1: j <= ceil((e1 - cp - lead) / full) - 1
+    const int64_t x64 = e1 - cp - lead;
     int jmax = 0;
     if (x64 > 0) {
       const int x = x64 < 0x7fffffff ? static_cast<int>(x64) : 0x7fffffff;
@@ -311,7 +324,7 @@ struct Schedule {
       s.cfirst = -1;
     } else {
       s.cfirst = cta_of(cp);
-      s.nseg = cta_of(tile_start(cp, n - 1)) - s.cfirst + 1;
+      s.nseg = cta_of(tile_start(cp, lead, n - 1)) - s.cfirst + 1;
     }
     return true;
   }
@@ -331,7 +344,7 @@ struct Schedule {
     const int64_t cp = pair_start(pair);
     int j0 = 0;
     if (e0 > cp) {
-      const int64_t x = e0 - cp - cm.seg;
+      const int64_t x = e0 - cp - cm.lead(len_of(lo));
       j0 = static_cast<int>(x > 0 ? ceil_div_u32(x, cm.full()) : 1);
       if (j0 < 1) j0 = 1;
     }
@@ -549,7 +562,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     uint4* z = reinterpret_cast<uint4*>(pbufs);
     for (int i = tid; i < 2 * G::kPBufBytes / 16; i += kSm100Threads) z[i] = make_uint4(0, 0, 0, 0);
   }
-  const CostModel cm{p.cost_tile, p.cost_seg};
+  const CostModel cm{p.cost_tile, p.cost_seg, p.cost_floor};
   pdl_wait_prerequisites();
   // The epoch load is issued here and consumed after the sequence lengths'
   // loads, so the two round trips overlap.
@@ -584,10 +597,10 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   // align_tiles tiles per CTA — each CTA takes m whole pairs: no pair is
   // cut, so no partial, arrival counter or merge lengthens a launch whose
   // whole time is its latency chain.  Every pair then costs the same
-  // `aligned_cost` (more than its tiles' starts need: seg + (align_tiles - 1)
+  // `aligned_cost` (more than its tiles' starts need: lead + (align_tiles - 1)
   // full tiles) and range c is exactly pairs [m c, m (c + 1)).
   const bool aligned = short_pairs && align_max_tiles > 0;
-  const int aligned_cost = cm.seg + p.align_tiles * cm.full() + 1;
+  const int aligned_cost = cm.max_lead() + p.align_tiles * cm.full() + 1;
   if (warp == 0) {  // inclusive scan of pair costs -> exclusive prefix sums
     int carry = 0;
     for (int base = 1; base <= batch; base += 32) {
@@ -615,7 +628,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   sched.batch = batch;
   sched.hkv = hkv;
   sched.cm = cm;
-  // Each CTA's cost range is longer than the costliest tile (seg + full), so
+  // Each CTA's cost range is longer than the costliest tile (lead + full), so
   // every range holds at least one tile start: no CTA inside a pair's span is
   // empty, which the nseg count relies on.  CTAs past that (the host sized
   // the grid from an upper bound) have nothing to do.
@@ -624,7 +637,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   if (aligned) {
     sched.grid = static_cast<int>(ceil_div_u32(n_pairs, align_m));
   } else {
-    const int64_t g = div_u32(sched.total, cm.seg + cm.full() + 1);
+    const int64_t g = div_u32(sched.total, cm.max_lead() + cm.full() + 1);
     sched.grid = static_cast<int>(g < 1 ? 1 : (g < gridDim.x ? g : gridDim.x));
   }
   const int64_t range_end = sched.range_start(cta + 1);

@@ -56,6 +56,7 @@ struct DecodeParams {
   int len_add;                // keys appended this step: attended length = max(seqlens[b], 0) + len_add
   int cost_tile, cost_seg;    // split cost model: fixed cost per tile and per pair, in
                               // units where a full tile's K/V bytes cost 8
+  int cost_floor;             // least cost of a pair (its per-pair part is raised to reach it)
   int align_tiles;            // pair-aligned split when B * Hkv <= grid and every
                               // sequence has at most this many tiles (0: never)
   // e4m3 K/V only: dequantisation scales per KV head (K = k8 * k_scale[h],

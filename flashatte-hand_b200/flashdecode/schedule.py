@@ -10,9 +10,11 @@ page ranges (:664-671).
 
 Cost model (integer units, a full 128-token tile's K/V bytes = 8): a tile
 adds ``tile_fixed``; a sequence's partial last tile costs its 16-token boxes
-instead of 8; every (sequence, KV head) pair adds ``seg``.  Pairs are laid end
-to end (b-major, then KV head) and CTA c takes the tiles whose start cost is
-in [C*c/G, C*(c+1)/G).
+instead of 8; every (sequence, KV head) pair adds ``seg``, raised where
+needed so that no pair costs less than ``floor`` (the pair's ``lead``: its
+first tile starts at the pair's start, tile j >= 1 at start + lead + j *
+full).  Pairs are laid end to end (b-major, then KV head) and CTA c takes the
+tiles whose start cost is in [C*c/G, C*(c+1)/G).
 """
 from __future__ import annotations
 
@@ -23,10 +25,12 @@ MAX_BATCH_PER_LAUNCH = 512
 FULL_TILE = 8
 DEFAULT_TILE_FIXED = 2
 DEFAULT_SEG = 12
+DEFAULT_FLOOR = 40
 # e4m3 caches (half the bytes per tile for the same fixed work, plus the
 # in-kernel query split per pair): the kernel's defaults for that path
 E4M3_TILE_FIXED = 8
 E4M3_SEG = 48
+E4M3_FLOOR = 0
 # pair-aligned split: one whole pair per CTA when B * Hkv <= grid and no
 # sequence has more than this many tiles
 DEFAULT_ALIGN_TILES = 16
@@ -55,33 +59,45 @@ def tiles_of(length: int, max_len: int | None = None) -> int:
     return (L + TILE_TOKENS - 1) // TILE_TOKENS if L > 0 else 1
 
 
-def pair_cost(length: int, tile_fixed: int = DEFAULT_TILE_FIXED, seg: int = DEFAULT_SEG) -> int:
+def tiles_cost(length: int, tile_fixed: int = DEFAULT_TILE_FIXED) -> int:
     L = max(0, int(length))
     n_full, rem = divmod(L, TILE_TOKENS)
     tail = ((rem + 15) // 16 + tile_fixed) if (rem > 0 or L == 0) else 0
-    return seg + n_full * (FULL_TILE + tile_fixed) + tail
+    return n_full * (FULL_TILE + tile_fixed) + tail
+
+
+def lead(length: int, tile_fixed: int = DEFAULT_TILE_FIXED, seg: int = DEFAULT_SEG,
+         floor: int = DEFAULT_FLOOR) -> int:
+    return max(seg, floor - tiles_cost(length, tile_fixed))
+
+
+def pair_cost(length: int, tile_fixed: int = DEFAULT_TILE_FIXED, seg: int = DEFAULT_SEG,
+              floor: int = DEFAULT_FLOOR) -> int:
+    return lead(length, tile_fixed, seg, floor) + tiles_cost(length, tile_fixed)
 
 
 def segments(seqlens, hkv: int, grid: int, max_len: int | None = None,
              tile_fixed: int = DEFAULT_TILE_FIXED, seg: int = DEFAULT_SEG,
-             align_tiles: int = 0) -> list[Segment]:
+             align_tiles: int = 0, floor: int = DEFAULT_FLOOR) -> list[Segment]:
     """All segments of all CTAs, in CTA order then work order (kernel's split).
 
     align_tiles > 0: with m = ceil(B * Hkv / grid) pairs per CTA, when no
     sequence has more than align_tiles // m tiles, every pair costs the same
-    (seg + align_tiles full tiles + 1) and CTA c takes exactly the whole
+    (max lead + align_tiles full tiles + 1) and CTA c takes exactly the whole
     pairs [m c, m (c + 1))."""
     lens = [min(max(0, int(L)), max_len) if max_len is not None else max(0, int(L)) for L in seqlens]
     full = FULL_TILE + tile_fixed
     npairs = len(lens) * hkv
     m = -(-npairs // grid)
     aligned = align_tiles // m > 0 and all(tiles_of(L) <= align_tiles // m for L in lens)
-    k_aligned = seg + align_tiles * full + 1
+    max_lead = max(seg, floor)
+    k_aligned = max_lead + align_tiles * full + 1
+    leads = [lead(L, tile_fixed, seg, floor) for L in lens]
     prefix = [0]
     for L in lens:
-        prefix.append(prefix[-1] + (k_aligned if aligned else pair_cost(L, tile_fixed, seg)))
+        prefix.append(prefix[-1] + (k_aligned if aligned else pair_cost(L, tile_fixed, seg, floor)))
     total = hkv * prefix[-1]
-    grid = -(-npairs // m) if aligned else max(1, min(grid, total // (seg + full + 1)))
+    grid = -(-npairs // m) if aligned else max(1, min(grid, total // (max_lead + full + 1)))
 
     def range_start(c):
         if aligned:
@@ -95,20 +111,21 @@ def segments(seqlens, hkv: int, grid: int, max_len: int | None = None,
         b, kvh = divmod(pair, hkv)
         return hkv * prefix[b] + kvh * (prefix[b + 1] - prefix[b])
 
-    def tile_start(cp, j):
-        return cp if j == 0 else cp + seg + j * full
+    def tile_start(cp, ld, j):
+        return cp if j == 0 else cp + ld + j * full
 
     def make(c, pair, j0, e1):
         b, kvh = divmod(pair, hkv)
         n = tiles_of(lens[b])
+        ld = leads[b]
         cp = pair_start(pair)
-        if j0 >= n or tile_start(cp, j0) >= e1:
+        if j0 >= n or tile_start(cp, ld, j0) >= e1:
             return None
-        x = e1 - cp - seg
+        x = e1 - cp - ld
         jmax = -(-x // full) - 1 if x > 0 else 0
         jmax = min(jmax, n - 1)
         c0 = cta_of(cp)
-        return Segment(c, b, kvh, pair, j0, jmax - j0 + 1, cta_of(tile_start(cp, n - 1)) - c0 + 1, c0)
+        return Segment(c, b, kvh, pair, j0, jmax - j0 + 1, cta_of(tile_start(cp, ld, n - 1)) - c0 + 1, c0)
 
     out: list[Segment] = []
     for c in range(grid):
@@ -126,7 +143,7 @@ def segments(seqlens, hkv: int, grid: int, max_len: int | None = None,
         cp = pair_start(pair)
         j0 = 0
         if e0 > cp:
-            x = e0 - cp - seg
+            x = e0 - cp - leads[lo]
             j0 = max(1, -(-x // full)) if x > 0 else 1
         s = make(c, pair, j0, e1)
         if s is None and pair + 1 < npairs:

@@ -79,11 +79,13 @@ def test_lpt_partition_balances_skew(world):
     ([300, 7], 8, 148), ([1, 127, 128, 129, 300, 0, 1000, 2049], 4, 148),
     ([1, 127, 128, 129, 300, 0, 1000, 2049], 1, 148),
 ])
-@pytest.mark.parametrize("weights", ["16-bit", "e4m3"])
+@pytest.mark.parametrize("weights", ["16-bit", "e4m3", "no-floor", "high-floor"])
 @pytest.mark.parametrize("align", [0, schedule.DEFAULT_ALIGN_TILES, 64])
 def test_schedule_covers_every_tile_once(seqlens, hkv, grid, weights, align):
-    kw = (dict(tile_fixed=schedule.E4M3_TILE_FIXED, seg=schedule.E4M3_SEG) if weights == "e4m3"
-          else {})
+    kw = {"16-bit": {}, "e4m3": dict(tile_fixed=schedule.E4M3_TILE_FIXED, seg=schedule.E4M3_SEG,
+                                     floor=schedule.E4M3_FLOOR),
+          # no floor, and one far above a few tiles' cost
+          "no-floor": dict(seg=12, floor=0), "high-floor": dict(seg=18, floor=300)}[weights]
     kw["align_tiles"] = align
     segs = schedule.segments(seqlens, hkv, grid, **kw)
     seen = {}
@@ -135,12 +137,23 @@ def test_pair_aligned_split_several_pairs_per_cta(seqlens, hkv, m):
         assert any(s.nseg > 1 for s in segs)
 
 
+def test_cost_floor_raises_short_pairs_only():
+    """A pair never costs less than the floor; pairs above it keep seg."""
+    for L in [0, 1, 127, 128, 129, 300, 1000, 5000]:
+        base = schedule.pair_cost(L, seg=12, floor=0)
+        raised = schedule.pair_cost(L, seg=12, floor=40)
+        assert raised == max(base, 40)
+        assert schedule.lead(L, seg=12, floor=40) >= 12
+    assert schedule.pair_cost(5000, seg=12, floor=40) == schedule.pair_cost(5000, seg=12, floor=0)
+    assert schedule.pair_cost(1, seg=12, floor=0) < 40 == schedule.pair_cost(1, seg=12, floor=40)
+
+
 def _cta_costs(seqlens, hkv, grid):
     full = schedule.FULL_TILE + schedule.DEFAULT_TILE_FIXED
     costs = {}
     for s in schedule.segments(seqlens, hkv, grid):
         L = max(0, int(seqlens[s.b]))
-        c = schedule.DEFAULT_SEG if s.tile0 == 0 else 0
+        c = schedule.lead(L) if s.tile0 == 0 else 0
         for j in range(s.tile0, s.tile0 + s.ntiles):
             rem = L - j * schedule.TILE_TOKENS
             c += full if rem >= schedule.TILE_TOKENS else (rem + 15) // 16 + schedule.DEFAULT_TILE_FIXED
@@ -153,7 +166,8 @@ def test_schedule_balances_estimated_cost(idx):
     c = cases.config_case(idx)
     costs = _cta_costs(c.seqlens.tolist(), c.Hkv, 148)
     assert len(costs) == 148
-    item = schedule.DEFAULT_SEG + schedule.FULL_TILE + schedule.DEFAULT_TILE_FIXED
+    item = (max(schedule.DEFAULT_SEG, schedule.DEFAULT_FLOOR) + schedule.FULL_TILE
+            + schedule.DEFAULT_TILE_FIXED)
     assert max(costs.values()) - min(costs.values()) <= 2 * item
 
 
@@ -198,6 +212,7 @@ def test_cost_defaults_match_the_host_library():
     got = {m.group(1): int(m.group(2))
            for m in re.finditer(r"constexpr int (kDefaultCost\w+) = (\d+);", src)}
     assert got == {"kDefaultCostTile": schedule.DEFAULT_TILE_FIXED, "kDefaultCostSeg": schedule.DEFAULT_SEG,
-                   "kDefaultCostTile8": schedule.E4M3_TILE_FIXED, "kDefaultCostSeg8": schedule.E4M3_SEG}
+                   "kDefaultCostTile8": schedule.E4M3_TILE_FIXED, "kDefaultCostSeg8": schedule.E4M3_SEG,
+                   "kDefaultCostFloor": schedule.DEFAULT_FLOOR}
     align = re.search(r"constexpr int kDefaultAlignTiles = (\d+);", src)
     assert int(align.group(1)) == schedule.DEFAULT_ALIGN_TILES
