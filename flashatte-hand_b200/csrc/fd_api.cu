@@ -50,6 +50,7 @@ constexpr int kDefaultCostSeg8 = 48;
 // their cost and their times.  A larger seg for every pair gains about as
 // much on config 3 but slows the page-16 config 5 mixes.
 constexpr int kDefaultCostFloor = 40;
+constexpr int kDefaultCostFloor8 = 0;
 // Pair-aligned split (one whole (sequence, KV head) pair per CTA) for
 // launches with no more pairs than SMs and no sequence longer than this
 // many 128-token tiles (see the schedule set-up in fd_decode_sm100.cuh).
@@ -208,7 +209,7 @@ int64_t seqs_per_launch(int64_t per_seq_cost, int64_t aligned_cost, int64_t hkv,
 int esize(int dtype) { return dtype == FD_DTYPE_FP32 ? 4 : 2; }
 
 // Tuning knobs (FD_TMA_CHUNK, FD_COST_TILE / FD_COST_SEG / FD_COST_FLOOR and
-// the e4m3 twins of the first two, FD_ALIGN_TILES, FD_SIMT_MAX_TOKENS, FD_PDL, FD_WAIT_TIMEOUT_NS) are read from the
+// their e4m3 twins, FD_ALIGN_TILES, FD_SIMT_MAX_TOKENS, FD_PDL, FD_WAIT_TIMEOUT_NS) are read from the
 // environment only when
 // FD_DEBUG_KNOBS=1: without that switch a caller's environment cannot change
 // the schedule or the timeouts of the operator.
@@ -318,14 +319,14 @@ int cost_seg(bool kv8 = false) {
   return kv8 ? v8 : v;
 }
 
-// 16-bit caches only (e4m3 launches use no floor).
-int cost_floor() {
+int cost_floor(bool kv8 = false) {
   static const int v = env_int("FD_COST_FLOOR", kDefaultCostFloor, 0, 1024);
-  return v;
+  static const int v8 = env_int("FD_COST_FLOOR8", kDefaultCostFloor8, 0, 1024);
+  return kv8 ? v8 : v;
 }
 // Largest per-pair part (`lead`) of any pair under the cost model.
 int64_t max_lead(bool kv8 = false) {
-  const int floor = kv8 ? 0 : cost_floor();
+  const int floor = cost_floor(kv8);
   return cost_seg(kv8) > floor ? cost_seg(kv8) : floor;
 }
 
@@ -938,11 +939,11 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
     if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "K/V tensor map encode failed (%d)", (int)r);
   }
   const int64_t per_seq_cost =
-      cost_seg(true) + ((kv_max + fd::kTileTokens - 1) / fd::kTileTokens + 1) *
+      max_lead(true) + ((kv_max + fd::kTileTokens - 1) / fd::kTileTokens + 1) *
                        (8 + static_cast<int64_t>(cost_tile(true)));
   const int64_t per_launch = seqs_per_launch(
       per_seq_cost,
-      cost_seg(true) + static_cast<int64_t>(align_tiles()) * (8 + cost_tile(true)) + 1,
+      max_lead(true) + static_cast<int64_t>(align_tiles()) * (8 + cost_tile(true)) + 1,
       num_heads_k, sms);
   if (per_launch == 0) return set_error(FD_ERR_UNSUPPORTED, "sequence too long");
   if (xa != nullptr && per_launch < batch_size)
@@ -978,7 +979,7 @@ static int decode_kv8_impl(const void* q, const void* k_cache, const void* v_cac
     p.align_tiles = align_tiles();
     p.cost_tile = cost_tile(true);
     p.cost_seg = cost_seg(true);
-    p.cost_floor = 0;
+    p.cost_floor = cost_floor(true);
     p.xworld = 0;
     p.pdl = (xa == nullptr && pdl_enabled()) ? 1 : 0;
     p.len_add = len_add;

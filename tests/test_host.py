@@ -213,6 +213,6 @@ def test_cost_defaults_match_the_host_library():
            for m in re.finditer(r"constexpr int (kDefaultCost\w+) = (\d+);", src)}
     assert got == {"kDefaultCostTile": schedule.DEFAULT_TILE_FIXED, "kDefaultCostSeg": schedule.DEFAULT_SEG,
                    "kDefaultCostTile8": schedule.E4M3_TILE_FIXED, "kDefaultCostSeg8": schedule.E4M3_SEG,
-                   "kDefaultCostFloor": schedule.DEFAULT_FLOOR}
+                   "kDefaultCostFloor": schedule.DEFAULT_FLOOR, "kDefaultCostFloor8": schedule.E4M3_FLOOR}
     align = re.search(r"constexpr int kDefaultAlignTiles = (\d+);", src)
     assert int(align.group(1)) == schedule.DEFAULT_ALIGN_TILES
