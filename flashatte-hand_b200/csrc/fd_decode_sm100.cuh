@@ -719,16 +719,13 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         const int nbox = tail ? (valid_rows > 0 ? (valid_rows + 15) / 16 : 0) : nchunks;
         const int pos = tok0 + lane * box;
         const bool need = lane < nbox;
+        // Issued before the wait for the stage and first used after it, so the
+        // page-table round trip overlaps the wait.  With 16-token pages a tile
+        // reads eight new entries; checking them here, before the wait, put
+        // that round trip on the producer's path (config 5 ran 8 % slower,
+        // 10 % with an e4m3 cache).
         int page_id = 0;
-        if (need) page_id = __ldg(bt_row + pos / p.page);  // issued before the wait
-        if (need && (page_id < 0 || page_id >= p.num_blocks)) {
-          // A page id inside the sequence's range that is not in the pool:
-          // report it and fetch a box that lies wholly past the pool instead,
-          // which the tensor copy fills with zeros (no access outside the
-          // cache; those keys score 0 and their values add 0).
-          report_status(p.err, kStatusBadPage);
-          page_id = static_cast<int>(p.num_blocks);
-        }
+        if (need) page_id = __ldg(bt_row + pos / p.page);
         const int stage = static_cast<int>(it % G::kStages);
         ok = lane0_wait(&ring_empty[stage], static_cast<uint32_t>((it / G::kStages) & 1) ^ 1u,
                         abort_flag, budget, lane);
@@ -771,6 +768,14 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         }
         __syncwarp();
         if (need) {
+          if (page_id < 0 || page_id >= p.num_blocks) {
+            // A page id inside the sequence's range that is not in the pool:
+            // report it and fetch a box that lies wholly past the pool
+            // instead, which the tensor copy fills with zeros (no access
+            // outside the cache; those keys score 0 and their values add 0).
+            report_status(p.err, kStatusBadPage);
+            page_id = static_cast<int>(p.num_blocks);
+          }
           const int off = pos % p.page;
           const CUtensorMap* m = tail ? map_tail : map_full;
           uint8_t* dst = sdst + operand_off + lane * box * 128;
