@@ -148,6 +148,25 @@ def test_cost_floor_raises_short_pairs_only():
     assert schedule.pair_cost(1, seg=12, floor=0) < 40 == schedule.pair_cost(1, seg=12, floor=40)
 
 
+def test_cost_floor_caps_pairs_per_cta_on_skewed_shards():
+    """Config 3 split over 8 ranks: with the per-pair cost alone some CTAs
+    take up to 17 short pairs (the slowest shard measured on a B200 was the
+    one with 17); the floor spreads them to at most 8 per CTA without
+    changing the tiles a CTA streams by more than one."""
+    from flashdecode import dist as fdist
+    c = cases.config_case(3)
+    worst_seg_only = 0
+    for rank in range(8):
+        sh = fdist.batch_shard(c, rank, 8)[0]
+        sl = sh.seqlens.tolist()
+        seg_only = schedule.split_stats(sl, sh.Hkv, 148, floor=0, align_tiles=16)
+        floored = schedule.split_stats(sl, sh.Hkv, 148, align_tiles=16)
+        worst_seg_only = max(worst_seg_only, seg_only["segments_per_cta_max"])
+        assert floored["segments_per_cta_max"] <= 8
+        assert floored["tiles_per_cta_max"] <= seg_only["tiles_per_cta_max"] + 1
+    assert worst_seg_only >= 16
+
+
 def _cta_costs(seqlens, hkv, grid):
     full = schedule.FULL_TILE + schedule.DEFAULT_TILE_FIXED
     costs = {}
